@@ -1,0 +1,376 @@
+// Host side of the C ABI declared in include/gqa_fa_b200.h: argument
+// validation, TMA tensor-map encoding, per-head_dim kernel configuration and
+// launches. Tile shapes are fixed per head_dim (there is no runtime tuning):
+//
+//   head_dim 256  forward  M=128 BN=128, one 256-column O chunk
+//                 dQ, dK   M=128 BN=128, single-buffered scores (TMEM: 256+128+128)
+//                 dV       M=128 BN=128, double-buffered scores
+//   head_dim 512  forward  M=128 BN=128, two 256-column O chunks (grid dimension)
+//                 dQ/dK/dV M=64  BN=64, accumulator in the lower TMEM half-quadrants
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/gqa_fa_b200.h"
+#include "attn_kernel.cuh"
+
+namespace gqafa {
+
+__device__ int g_status_word;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn get_encode() {
+  static std::once_flag once;
+  static EncodeFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  return fn;
+}
+
+struct TensorDesc {
+  const void* ptr;
+  long long sb, sh, sn;  // element strides, d stride == 1
+  int H;
+};
+
+// Validate one [B, H, N, D] tensor and return TMA-legal strides.
+int check_tensor(const char* name, const void* ptr, const long long* st, int B, int H, int N, int D,
+                 TensorDesc* out) {
+  if (ptr == nullptr) return fail(GQAFA_ERR_INVALID, "%s: null pointer", name);
+  if (st == nullptr) return fail(GQAFA_ERR_INVALID, "%s: null strides", name);
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+    return fail(GQAFA_ERR_INVALID, "%s: data pointer must be 16-byte aligned", name);
+  if (st[3] != 1) return fail(GQAFA_ERR_INVALID, "%s: last (head_dim) stride must be 1, got %lld", name, st[3]);
+  long long sn = st[2], sh = st[1], sb = st[0];
+  // Size-1 dims may carry any stride in torch; give TMA a natural one.
+  if (N == 1) sn = D;
+  if (H == 1) sh = sn * N;
+  if (B == 1) sb = sh * H;
+  const long long s3[3] = {sn, sh, sb};
+  for (int i = 0; i < 3; ++i) {
+    if (s3[i] <= 0 || s3[i] % 8 != 0)
+      return fail(GQAFA_ERR_INVALID,
+                  "%s: strides must be positive multiples of 8 elements (16 bytes), got "
+                  "(%lld, %lld, %lld, %lld)",
+                  name, st[0], st[1], st[2], st[3]);
+    if (s3[i] * 2 >= (1LL << 40)) return fail(GQAFA_ERR_INVALID, "%s: stride too large for TMA", name);
+  }
+  out->ptr = ptr;
+  out->sb = sb;
+  out->sh = sh;
+  out->sn = sn;
+  out->H = H;
+  return GQAFA_OK;
+}
+
+int encode_map(CUtensorMap* m, const TensorDesc& t, int B, int N, int D, int box_rows, bool bf16) {
+  EncodeFn enc = get_encode();
+  if (!enc) return fail(GQAFA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)N, (cuuint64_t)t.H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)(t.sn * 2), (cuuint64_t)(t.sh * 2), (cuuint64_t)(t.sb * 2)};
+  cuuint32_t box[4] = {64u, (cuuint32_t)box_rows, 1u, 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void*>(t.ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GQAFA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return GQAFA_OK;
+}
+
+int* status_ptr() {
+  static std::mutex mu;
+  static int* ptrs[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+template <class C>
+int launch(const CUtensorMap (&maps)[5], KParams p, cudaStream_t stream) {
+  static std::atomic<unsigned long long> attr_done_mask{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(GQAFA_ERR_CUDA, "cudaGetDevice failed");
+  const unsigned long long bit = 1ULL << (dev & 63);
+  if (!(attr_done_mask.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES);
+    if (e != cudaSuccess) return fail(GQAFA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attr_done_mask.fetch_or(bit);
+  }
+  p.num_row_tiles = (p.N + C::M - 1) / C::M;
+  const long long heads = C::ROWS_ARE_Q ? p.Hq : p.Hkv;
+  const long long grid = (long long)p.num_row_tiles * heads * p.B * C::NCHUNK;
+  if (grid <= 0 || grid > 0x7fffffffLL) return fail(GQAFA_ERR_INVALID, "grid size %lld out of range", grid);
+  attn_kernel<C><<<(unsigned)grid, 256, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(GQAFA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return GQAFA_OK;
+}
+
+// Fixed configurations. Cfg<ROLE, M, D, DC, BN, NS, NSTAGES, YGROUP, BF16>
+template <bool BF16> using Fwd256 = Cfg<ROLE_FWD, 128, 256, 256, 128, 2, 8, 4, BF16>;
+template <bool BF16> using Dq256 = Cfg<ROLE_DQ, 128, 256, 256, 128, 1, 6, 2, BF16>;
+template <bool BF16> using Dk256 = Cfg<ROLE_DK, 128, 256, 256, 128, 1, 6, 2, BF16>;
+template <bool BF16> using Dv256 = Cfg<ROLE_DV, 128, 256, 256, 128, 2, 8, 4, BF16>;
+template <bool BF16> using Fwd512 = Cfg<ROLE_FWD, 128, 512, 256, 128, 2, 6, 2, BF16>;
+template <bool BF16> using Dq512 = Cfg<ROLE_DQ, 64, 512, 512, 64, 2, 8, 4, BF16>;
+template <bool BF16> using Dk512 = Cfg<ROLE_DK, 64, 512, 512, 64, 2, 8, 4, BF16>;
+template <bool BF16> using Dv512 = Cfg<ROLE_DV, 64, 512, 512, 64, 2, 12, 4, BF16>;
+
+struct Problem {
+  int B, Hq, Hkv, N, D, causal, window;
+  float scale;
+  bool bf16;
+};
+
+int check_problem(int B, int Hq, int Hkv, int N, int D, float scale, int causal, int window, int dtype,
+                  Problem* pr) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || N <= 0)
+    return fail(GQAFA_ERR_INVALID, "sizes must be positive (B=%d H_Q=%d H_KV=%d N=%d)", B, Hq, Hkv, N);
+  if (Hq % Hkv != 0) return fail(GQAFA_ERR_INVALID, "H_Q (%d) must be a multiple of H_KV (%d)", Hq, Hkv);
+  if (dtype != GQAFA_DTYPE_FP16 && dtype != GQAFA_DTYPE_BF16)
+    return fail(GQAFA_ERR_INVALID, "dtype code %d is not fp16 (0) or bf16 (1)", dtype);
+  if (D != 256 && D != 512)
+    return fail(GQAFA_ERR_UNSUPPORTED, "head_dim %d is not implemented on sm_100a (supported: 256, 512)", D);
+  if (!(scale > 0.f) || !std::isfinite(scale))
+    return fail(GQAFA_ERR_INVALID, "softmax_scale must be positive and finite");
+  if (window < 0) return fail(GQAFA_ERR_INVALID, "window must be >= 0");
+  pr->B = B;
+  pr->Hq = Hq;
+  pr->Hkv = Hkv;
+  pr->N = N;
+  pr->D = D;
+  pr->causal = causal ? 1 : 0;
+  // Reference semantics: the window only applies to causal attention and a
+  // window covering the whole sequence is plain causal.
+  pr->window = (pr->causal && window > 0 && window < N) ? window : 0;
+  pr->scale = scale;
+  pr->bf16 = (dtype == GQAFA_DTYPE_BF16);
+  return GQAFA_OK;
+}
+
+KParams base_params(const Problem& pr) {
+  KParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.B = pr.B;
+  p.Hq = pr.Hq;
+  p.Hkv = pr.Hkv;
+  p.N = pr.N;
+  p.G = pr.Hq / pr.Hkv;
+  p.causal = pr.causal;
+  p.window = pr.window;
+  p.scale = pr.scale;
+  p.scale_log2 = pr.scale * 1.4426950408889634f;
+  return p;
+}
+
+void set_out(KParams& p, void* ptr, const TensorDesc& t) {
+  p.out = ptr;
+  p.out_sb = t.sb;
+  p.out_sh = t.sh;
+  p.out_sn = t.sn;
+}
+
+template <bool BF16, class CF>
+int fwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const TensorDesc& v, void* o,
+             const TensorDesc& od, float* lse, cudaStream_t st) {
+  CUtensorMap maps[5];
+  int rc;
+  if ((rc = encode_map(&maps[0], q, pr.B, pr.N, pr.D, CF::M, BF16))) return rc;
+  if ((rc = encode_map(&maps[2], k, pr.B, pr.N, pr.D, CF::BN, BF16))) return rc;
+  if ((rc = encode_map(&maps[4], v, pr.B, pr.N, pr.D, CF::BN, BF16))) return rc;
+  maps[1] = maps[0];
+  maps[3] = maps[2];
+  KParams p = base_params(pr);
+  set_out(p, o, od);
+  p.lse = lse;
+  p.status = status_ptr();
+  if (!p.status) return fail(GQAFA_ERR_CUDA, "cannot resolve the device status word");
+  return launch<CF>(maps, p, st);
+}
+
+template <bool BF16, class CQ, class CK, class CV>
+int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const TensorDesc& v,
+             const TensorDesc& o, const TensorDesc& dout, const float* lse, void* dq, const TensorDesc& dqd,
+             void* dk, const TensorDesc& dkd, void* dv, const TensorDesc& dvd, float* delta, cudaStream_t st) {
+  int* status = status_ptr();
+  if (!status) return fail(GQAFA_ERR_CUDA, "cannot resolve the device status word");
+  int rc;
+  {  // dQ + delta
+    CUtensorMap maps[5];
+    if ((rc = encode_map(&maps[0], q, pr.B, pr.N, pr.D, CQ::M, BF16))) return rc;
+    if ((rc = encode_map(&maps[1], dout, pr.B, pr.N, pr.D, CQ::M, BF16))) return rc;
+    if ((rc = encode_map(&maps[2], k, pr.B, pr.N, pr.D, CQ::BN, BF16))) return rc;
+    if ((rc = encode_map(&maps[3], v, pr.B, pr.N, pr.D, CQ::BN, BF16))) return rc;
+    maps[4] = maps[2];
+    KParams p = base_params(pr);
+    set_out(p, dq, dqd);
+    p.lse = const_cast<float*>(lse);
+    p.delta = delta;
+    p.o = o.ptr;
+    p.o_sb = o.sb;
+    p.o_sh = o.sh;
+    p.o_sn = o.sn;
+    p.dout = dout.ptr;
+    p.do_sb = dout.sb;
+    p.do_sh = dout.sh;
+    p.do_sn = dout.sn;
+    p.status = status;
+    if ((rc = launch<CQ>(maps, p, st))) return rc;
+  }
+  {  // dK
+    CUtensorMap maps[5];
+    if ((rc = encode_map(&maps[0], k, pr.B, pr.N, pr.D, CK::M, BF16))) return rc;
+    if ((rc = encode_map(&maps[1], v, pr.B, pr.N, pr.D, CK::M, BF16))) return rc;
+    if ((rc = encode_map(&maps[2], q, pr.B, pr.N, pr.D, CK::BN, BF16))) return rc;
+    if ((rc = encode_map(&maps[3], dout, pr.B, pr.N, pr.D, CK::BN, BF16))) return rc;
+    maps[4] = maps[2];
+    KParams p = base_params(pr);
+    set_out(p, dk, dkd);
+    p.lse = const_cast<float*>(lse);
+    p.delta = delta;
+    p.status = status;
+    if ((rc = launch<CK>(maps, p, st))) return rc;
+  }
+  {  // dV
+    CUtensorMap maps[5];
+    if ((rc = encode_map(&maps[0], k, pr.B, pr.N, pr.D, CV::M, BF16))) return rc;
+    if ((rc = encode_map(&maps[2], q, pr.B, pr.N, pr.D, CV::BN, BF16))) return rc;
+    if ((rc = encode_map(&maps[4], dout, pr.B, pr.N, pr.D, CV::BN, BF16))) return rc;
+    maps[1] = maps[0];
+    maps[3] = maps[2];
+    KParams p = base_params(pr);
+    set_out(p, dv, dvd);
+    p.lse = const_cast<float*>(lse);
+    p.delta = delta;
+    p.status = status;
+    if ((rc = launch<CV>(maps, p, st))) return rc;
+  }
+  return GQAFA_OK;
+}
+
+}  // namespace
+}  // namespace gqafa
+
+using namespace gqafa;
+
+extern "C" int gqafa_fwd(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+                         const void* v, const long long* v_strides, void* o, const long long* o_strides,
+                         float* lse, int batch, int heads_q, int heads_kv, int seqlen, int head_dim,
+                         float softmax_scale, int causal, int window, int dtype, void* stream) {
+  g_last_error.clear();
+  Problem pr;
+  int rc;
+  if ((rc = check_problem(batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, window, dtype, &pr)))
+    return rc;
+  TensorDesc qd, kd, vd, od;
+  if ((rc = check_tensor("q", q, q_strides, batch, heads_q, seqlen, head_dim, &qd))) return rc;
+  if ((rc = check_tensor("k", k, k_strides, batch, heads_kv, seqlen, head_dim, &kd))) return rc;
+  if ((rc = check_tensor("v", v, v_strides, batch, heads_kv, seqlen, head_dim, &vd))) return rc;
+  if ((rc = check_tensor("o", o, o_strides, batch, heads_q, seqlen, head_dim, &od))) return rc;
+  if (lse != nullptr && reinterpret_cast<uintptr_t>(lse) % 4 != 0)
+    return fail(GQAFA_ERR_INVALID, "lse must be 4-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pr.D == 256)
+    return pr.bf16 ? fwd_impl<true, Fwd256<true>>(pr, qd, kd, vd, o, od, lse, st)
+                   : fwd_impl<false, Fwd256<false>>(pr, qd, kd, vd, o, od, lse, st);
+  return pr.bf16 ? fwd_impl<true, Fwd512<true>>(pr, qd, kd, vd, o, od, lse, st)
+                 : fwd_impl<false, Fwd512<false>>(pr, qd, kd, vd, o, od, lse, st);
+}
+
+extern "C" int gqafa_bwd(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+                         const void* v, const long long* v_strides, const void* o, const long long* o_strides,
+                         const void* dout, const long long* dout_strides, const float* lse, void* dq,
+                         const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
+                         const long long* dv_strides, float* delta, int batch, int heads_q, int heads_kv,
+                         int seqlen, int head_dim, float softmax_scale, int causal, int window, int dtype,
+                         void* stream) {
+  g_last_error.clear();
+  Problem pr;
+  int rc;
+  if ((rc = check_problem(batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, window, dtype, &pr)))
+    return rc;
+  TensorDesc qd, kd, vd, od, dod, dqd, dkd, dvd;
+  if ((rc = check_tensor("q", q, q_strides, batch, heads_q, seqlen, head_dim, &qd))) return rc;
+  if ((rc = check_tensor("k", k, k_strides, batch, heads_kv, seqlen, head_dim, &kd))) return rc;
+  if ((rc = check_tensor("v", v, v_strides, batch, heads_kv, seqlen, head_dim, &vd))) return rc;
+  if ((rc = check_tensor("o", o, o_strides, batch, heads_q, seqlen, head_dim, &od))) return rc;
+  if ((rc = check_tensor("dout", dout, dout_strides, batch, heads_q, seqlen, head_dim, &dod))) return rc;
+  if ((rc = check_tensor("dq", dq, dq_strides, batch, heads_q, seqlen, head_dim, &dqd))) return rc;
+  if ((rc = check_tensor("dk", dk, dk_strides, batch, heads_kv, seqlen, head_dim, &dkd))) return rc;
+  if ((rc = check_tensor("dv", dv, dv_strides, batch, heads_kv, seqlen, head_dim, &dvd))) return rc;
+  if (lse == nullptr || delta == nullptr) return fail(GQAFA_ERR_INVALID, "lse and delta must be non-null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pr.D == 256)
+    return pr.bf16 ? bwd_impl<true, Dq256<true>, Dk256<true>, Dv256<true>>(pr, qd, kd, vd, od, dod, lse, dq, dqd,
+                                                                            dk, dkd, dv, dvd, delta, st)
+                   : bwd_impl<false, Dq256<false>, Dk256<false>, Dv256<false>>(pr, qd, kd, vd, od, dod, lse, dq,
+                                                                               dqd, dk, dkd, dv, dvd, delta, st);
+  return pr.bf16 ? bwd_impl<true, Dq512<true>, Dk512<true>, Dv512<true>>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk,
+                                                                          dkd, dv, dvd, delta, st)
+                 : bwd_impl<false, Dq512<false>, Dk512<false>, Dv512<false>>(pr, qd, kd, vd, od, dod, lse, dq, dqd,
+                                                                             dk, dkd, dv, dvd, delta, st);
+}
+
+extern "C" int gqafa_supported(int head_dim, int dtype) {
+  return (head_dim == 256 || head_dim == 512) && (dtype == GQAFA_DTYPE_FP16 || dtype == GQAFA_DTYPE_BF16);
+}
+
+extern "C" const char* gqafa_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int gqafa_device_status(int device, int reset) {
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return -1;
+  if (cudaSetDevice(device) != cudaSuccess) return -1;
+  int value = -1;
+  if (cudaDeviceSynchronize() == cudaSuccess &&
+      cudaMemcpyFromSymbol(&value, g_status_word, sizeof(int)) == cudaSuccess) {
+    if (reset) {
+      const int zero = 0;
+      if (cudaMemcpyToSymbol(g_status_word, &zero, sizeof(int)) != cudaSuccess) value = -1;
+    }
+  } else {
+    value = -1;
+  }
+  cudaSetDevice(prev);
+  return value;
+}
+
+extern "C" const char* gqafa_version(void) { return "gqa-fa-b200 0.1.0 (sm_100a, tcgen05)"; }

@@ -1,0 +1,93 @@
+/*
+ * gqa_fa_b200.h - C ABI of the B200 (sm_100a) GQA flash-attention library.
+ *
+ * The library replaces the three Triton launches of the reference's training
+ * path and the one launch of its inference path (zzhhjjj/gemma-triton-flash-attn):
+ *
+ *   gqafa_fwd  <- FlashAttnGQAFunction.forward launch of _flash_attn_gqa_kernel
+ *                 with STORE_LSE=True          (flash_attn/attention.py:1454-1468)
+ *              <- attention_flash_gqa launch with STORE_LSE=False, lse == NULL
+ *                                              (flash_attn/attention.py:583-603)
+ *   gqafa_bwd  <- FlashAttnGQAFunction.backward: the dQ launch with the delta
+ *                 prologue (flash_attn/attention.py:1506-1523) followed by the
+ *                 packed dK/dV launch (flash_attn/attention.py:1602-1620)
+ *
+ * Conventions (all taken from the reference):
+ *   - q is [B, H_Q, N, D]; k, v are [B, H_KV, N, D]; H_Q % H_KV == 0 and query
+ *     head h reads KV head h / (H_Q / H_KV)   (attention.py:272).
+ *   - Tensors are fp16 or bf16 (dtype code below) with arbitrary strides in
+ *     elements, given as {stride_b, stride_h, stride_n, stride_d}; stride_d must
+ *     be 1, the others multiples of 8 elements (16 bytes), pointers 16-byte
+ *     aligned. Transposed views such as HF's [B, N, H, D] storage are accepted
+ *     without a copy.
+ *   - causal != 0 applies k <= q. window > 0 additionally applies q - k < window,
+ *     and only when causal != 0 (attention.py:289-293, 347-356). window >= N is
+ *     treated as full causal (attention.py:1442-1443).
+ *   - softmax_scale multiplies Q K^T. The reference fixes it at 1/sqrt(D)
+ *     (attention.py:1461); passing another value is how the HF adapter avoids
+ *     pre-multiplying q (hf_integration.py:55-58).
+ *   - lse is fp32 [B, H_Q, N] contiguous, natural log, including the scale
+ *     (attention.py:384-388). delta is fp32 [B, H_Q, N] contiguous scratch that
+ *     gqafa_bwd fills with rowsum(dO * O) (attention.py:738-742).
+ *   - Outputs have the dtype of q. dq/dk/dv have the shapes of q/k/v.
+ *   - Work is launched on `stream` (a cudaStream_t, NULL = legacy default) of
+ *     the current CUDA device; nothing is allocated and nothing synchronises.
+ *
+ * Return value: GQAFA_OK, or an error code; gqafa_last_error() then returns a
+ * message (thread-local).
+ */
+#ifndef GQA_FA_B200_H
+#define GQA_FA_B200_H
+
+#if defined(__GNUC__)
+#define GQAFA_API __attribute__((visibility("default")))
+#else
+#define GQAFA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GQAFA_DTYPE_FP16 0
+#define GQAFA_DTYPE_BF16 1
+
+#define GQAFA_OK 0
+#define GQAFA_ERR_INVALID 1     /* bad shape, stride, pointer or flag   */
+#define GQAFA_ERR_UNSUPPORTED 2 /* valid but not implemented (head_dim) */
+#define GQAFA_ERR_CUDA 3        /* a CUDA runtime / driver call failed   */
+
+/* Forward. lse may be NULL (inference path, no LSE written). */
+GQAFA_API int gqafa_fwd(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+              const void* v, const long long* v_strides, void* o, const long long* o_strides, float* lse,
+              int batch, int heads_q, int heads_kv, int seqlen, int head_dim, float softmax_scale,
+              int causal, int window, int dtype, void* stream);
+
+/* Backward. Reads q, k, v, o, dout and lse; writes dq, dk, dv and delta. */
+GQAFA_API int gqafa_bwd(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+              const void* v, const long long* v_strides, const void* o, const long long* o_strides,
+              const void* dout, const long long* dout_strides, const float* lse, void* dq,
+              const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
+              const long long* dv_strides, float* delta, int batch, int heads_q, int heads_kv,
+              int seqlen, int head_dim, float softmax_scale, int causal, int window, int dtype,
+              void* stream);
+
+/* 1 if (head_dim, dtype) has a compiled kernel set, else 0. */
+GQAFA_API int gqafa_supported(int head_dim, int dtype);
+
+/* Message of the last failed call on this thread ("" if none). */
+GQAFA_API const char* gqafa_last_error(void);
+
+/* Synchronises `device` and returns its kernel status word (0 = every kernel
+ * finished its pipeline; otherwise the code of the first bounded wait that
+ * timed out). reset != 0 clears the word afterwards. Returns -1 on a CUDA
+ * error. Not for the hot path. */
+GQAFA_API int gqafa_device_status(int device, int reset);
+
+/* Library version string. */
+GQAFA_API const char* gqafa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GQA_FA_B200_H */
