@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Headline benchmark: GQA flash-attention TFLOPS/s on B200.
+
+Workload (the north-star shape): Gemma-4-E2B global layer,
+B=1 per GPU, H_Q=32, H_KV=4, D=512, causal, N=16384, bf16, inputs seeded
+N(0,1)*0.5. One step = one forward + backward through the public autograd API
+(FlashAttnGQAFunction: 1 forward launch + 3 backward launches). FLOPs are
+charged by the reference's convention (fwd+bwd = 7*B*H*N^2*D).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU: weak scaling, each rank owns one
+batch element, i.e. the (b, kv-head-group) units of b = rank; there is no
+collective on the data path (the units are independent), so the timed region
+holds no communication. Timing: CUDA events on the launching stream, barrier +
+synchronize around the K timed steps, max over ranks. Q/dO are 512 MiB each,
+larger than the 126 MB L2, so no flush is needed between steps.
+
+`--impl reference` times the reference algorithm's CPU restatement (the
+oracle port; the reference itself is Python + Triton and has no native CPU
+path of its own beyond PyTorch eager) on this host's cores, on bounded
+samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "gemma-triton-flash-attn_b200")
+for _p in (ROOT, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "attn TFLOPS/s fwd & fwd+bwd (D=512 causal, D=256 SWA) at 1/2/4/8 B200"
+WORKLOADS = {
+    "cfg2": dict(name="gemma4-e2b global layer: GQA 32/4, D=512, causal, N=16384, bf16, fwd+bwd",
+                 B=1, Hq=32, Hkv=4, N=16384, D=512, causal=True, W=0, dtype=torch.bfloat16, factor=0.5),
+    "cfg3": dict(name="MoE sliding layer: GQA 16/8, D=256, causal SWA W=1024, N=16384, fp16, fwd+bwd",
+                 B=1, Hq=16, Hkv=8, N=16384, D=256, causal=True, W=1024, dtype=torch.float16, factor=1.0),
+    "cfg4": dict(name="MoE global layer: GQA 16/2, D=512, causal, N=16384, bf16, fwd+bwd (B=4 total)",
+                 B=4, Hq=16, Hkv=2, N=16384, D=512, causal=True, W=0, dtype=torch.bfloat16, factor=1.0),
+}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
+    ap.add_argument("--seqlen", type=int, default=None, help="override N (not the headline)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU seconds per sample")
+    ap.add_argument("--only", choices=["fwd", "dq", "dk", "dv"], default=None,
+                    help="profiling mode: run only this kernel, warmup + steps launches, print nothing")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return dict(tflops_burst=d.get("bf16_tflops"), tflops_sustained=d.get("bf16_tflops_sustained"),
+                    hbm_gbs=d.get("hbm_gbs"), source="measured")
+    return dict(tflops_burst=1590.0, tflops_sustained=1400.0, hbm_gbs=6650.0, source="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuids):
+        self.uuids = set(uuids)
+        self.proc = None
+        self.path = os.path.join("/tmp", f"gqafa_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+        return False
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        mhz, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            if self.uuids and parts[0] not in self.uuids:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, flag in zip(names, parts[4:8]):
+                if flag.lower().startswith("active"):
+                    reasons.add(n)
+        if not mhz:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo")
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+# ------------------------------------------------------------------ CPU leg
+def cpu_sample_run(wl, rows, seed=0):
+    """fwd+bwd of the oracle port on query head 0 of batch 0, query rows
+    [N-rows, N) against all keys (the heaviest causal rows). Returns
+    (seconds, charged FLOPs of the sample)."""
+    import numpy as np
+
+    from oracle.attention_oracle import attention_bwd, attention_fwd
+
+    N, D = wl["N"], wl["D"]
+    g = torch.Generator().manual_seed(seed)
+    mk = lambda *s: (torch.randn(*s, generator=g) * wl["factor"]).to(wl["dtype"]).float().numpy()  # noqa: E731
+    q = mk(1, 1, rows, D)
+    k = mk(1, 1, N, D)
+    v = mk(1, 1, N, D)
+    do = mk(1, 1, rows, D)
+    off = N - rows
+    t0 = time.perf_counter()
+    o, lse = attention_fwd(q, k, v, wl["causal"], wl["W"], q_offset=off, chunk=256)
+    attention_bwd(q, k, v, o, lse, do, wl["causal"], wl["W"], q_offset=off, chunk=256)
+    dt = time.perf_counter() - t0
+    W = wl["W"]
+    pairs = 0
+    for qpos in range(off, N):
+        lo = max(0, qpos - W + 1) if (wl["causal"] and W) else 0
+        hi = qpos + 1 if wl["causal"] else N
+        pairs += hi - lo
+    del np
+    return dt, 14 * D * pairs
+
+
+def cpu_calibrate(wl, target_s):
+    cpu_sample_run(wl, 256)  # warm the BLAS thread pool and allocator
+    t, _ = cpu_sample_run(wl, 256)
+    rows = int(256 * target_s / max(t, 1e-3))
+    rows = max(64, min(wl["N"], rows // 64 * 64))
+    return rows
+
+
+def cpu_baseline(wl, target_s, steps=1):
+    rows = cpu_calibrate(wl, target_s)
+    vals = []
+    for s in range(steps):
+        dt, fl = cpu_sample_run(wl, rows, seed=s)
+        vals.append(fl / dt / 1e12)
+    cores = os.cpu_count()
+    return dict(value=statistics.median(vals), unit="TFLOPS/s", cores=cores, kind="port",
+                sample=(f"oracle port (numpy fp32, {cores} BLAS threads): fwd+bwd of query head 0, "
+                        f"the last {rows} query rows of N={wl['N']} (D={wl['D']}) against all keys; "
+                        f"FLOPs charged 14*D*attended pairs"),
+                values=vals, rows=rows)
+
+
+# ------------------------------------------------------------------ GPU leg
+def make_inputs(wl, seed, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, Hq, Hkv, N, D = wl["B"], wl["Hq"], wl["Hkv"], wl["N"], wl["D"]
+    out = []
+    for shp in ((B, Hq, N, D), (B, Hkv, N, D), (B, Hkv, N, D), (B, Hq, N, D)):
+        x = torch.randn(shp, generator=g, device=device, dtype=torch.float32) * wl["factor"]
+        out.append(x.to(wl["dtype"]))
+        del x
+    return out
+
+
+def time_loop(fn, steps, stream):
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def run_ours(args, wl, world, rank, local):
+    from gemma_triton_flash_attn import FlashAttnGQAFunction, _lib
+    from gemma_triton_flash_attn.attention import _bwd, _fwd
+    from gemma_triton_flash_attn.flops import attn_flops, kernel_flops
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(device)
+    B, Hq, Hkv, N, D, causal, W = (wl[x] for x in ("B", "Hq", "Hkv", "N", "D", "causal", "W"))
+    window = W if (causal and 0 < W < N) else 0
+    scale = 1.0 / math.sqrt(D)
+    q, k, v, do = make_inputs(wl, 1234 + rank, device)
+    qg, kg, vg = (t.detach().requires_grad_(True) for t in (q, k, v))
+    if args.only:
+        o, lse = _fwd(q, k, v, causal, window, scale, True)
+        bufs = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
+                torch.empty((B, Hq, N), dtype=torch.float32, device=device))
+        if args.only != "fwd":
+            _bwd(q, k, v, o, lse, do, causal, window, scale, stage=0, out=bufs)  # delta for dK
+        torch.cuda.synchronize()
+        stage = {"dq": 0, "dk": 1, "dv": 2}.get(args.only)
+        for _ in range(args.warmup + args.steps):
+            if stage is None:
+                _fwd(q, k, v, causal, window, scale, True)
+            else:
+                _bwd(q, k, v, o, lse, do, causal, window, scale, stage=stage, out=bufs)
+        torch.cuda.synchronize()
+        if _lib.device_status(local) != 0:
+            raise RuntimeError("kernel status word set")
+        return
+
+    def step():
+        qg.grad = kg.grad = vg.grad = None
+        out = FlashAttnGQAFunction.apply(qg, kg, vg, causal, W)
+        out.backward(do)
+
+    flops_step = attn_flops(B, Hq, N, D, causal, window, bwd=True)
+    flops_fwd = attn_flops(B, Hq, N, D, causal, window)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    uuids = [uuid if uuid.startswith("GPU-") else "GPU-" + uuid]
+    with ClockSampler(uuids) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = time_loop(step, args.steps, stream)
+        barrier(world)
+    ms_max = max_over_ranks(ms, world, device)
+    value = world * flops_step / (ms_max * 1e-3) / 1e12
+
+    # forward alone (same launch as inside the step)
+    for _ in range(2):
+        _fwd(q, k, v, causal, window, scale, True)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_fwd = max_over_ranks(time_loop(lambda: _fwd(q, k, v, causal, window, scale, True), args.steps, stream),
+                            world, device)
+
+    # per-kernel timing for the roofline
+    o, lse = _fwd(q, k, v, causal, window, scale, True)
+    bufs = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
+            torch.empty((B, Hq, N), dtype=torch.float32, device=device))
+    kernels = {"fwd": ms_fwd}
+    for stage, name in enumerate(("dq", "dk", "dv")):
+        fn = lambda st=stage: _bwd(q, k, v, o, lse, do, causal, window, scale, stage=st, out=bufs)  # noqa: E731
+        fn()
+        torch.cuda.synchronize()
+        kernels[name] = time_loop(fn, args.steps, stream)
+    status = _lib.device_status(local)
+    dom = max(kernels, key=kernels.get)
+    peaks = measured_peaks()
+    kflops = kernel_flops(dom, B, Hq, N, D, causal, window)
+    achieved = kflops / (kernels[dom] * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get(f"{args.workload}:{dom}")
+    roofline = dict(bound="tensor", kernel=dom, achieved=round(achieved, 1), peak=peaks["tflops_sustained"],
+                    unit="TFLOP/s", frac=round(achieved / peaks["tflops_sustained"], 4), traffic=traffic,
+                    peak_kind=f"bf16_tflops_sustained ({peaks['source']}); burst {peaks['tflops_burst']}",
+                    flops_per_launch=kflops, ms_per_launch=round(kernels[dom], 3),
+                    kernel_ms={k_: round(v_, 3) for k_, v_ in kernels.items()},
+                    kernel_share={k_: round(v_ / sum(kernels.values()), 3) for k_, v_ in kernels.items()})
+
+    # end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq_, hk_, hv_, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
+        gq_h, gk_h, gv_h = (torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, k, v))
+        dq_, dk_, dv_ = (torch.empty_like(t) for t in (q, k, v))
+
+        def e2e_step():
+            with torch.no_grad():
+                dq_.copy_(hq_, non_blocking=True)
+                dk_.copy_(hk_, non_blocking=True)
+                dv_.copy_(hv_, non_blocking=True)
+                do.copy_(hdo, non_blocking=True)
+            qq, kk, vv = (t.detach().requires_grad_(True) for t in (dq_, dk_, dv_))
+            out = FlashAttnGQAFunction.apply(qq, kk, vv, causal, W)
+            out.backward(do)
+            gq_h.copy_(qq.grad, non_blocking=True)
+            gk_h.copy_(kk.grad, non_blocking=True)
+            gv_h.copy_(vv.grad, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        ms_e2e = max_over_ranks(time_loop(e2e_step, args.steps, stream), world, device)
+        h2d = sum(t.numel() * t.element_size() for t in (hq_, hk_, hv_, hdo))
+        d2h = sum(t.numel() * t.element_size() for t in (gq_h, gk_h, gv_h))
+        e2e = dict(value=round(world * flops_step / (ms_e2e * 1e-3) / 1e12, 2), unit="TFLOPS/s",
+                   ms_per_step=round(ms_e2e, 3), h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(wl, args.cpu_seconds, steps=1)
+        cpu.pop("values", None)
+
+    if rank == 0:
+        line = dict(
+            metric=METRIC, value=round(value, 2), unit="TFLOPS/s", n_gpus=world, steps=args.steps,
+            warmup=args.warmup, ms_per_step=round(ms_max, 3), higher_is_better=True, scaling="weak",
+            vs_baseline=None, dtype="bf16" if wl["dtype"] == torch.bfloat16 else "fp16",
+            data="synthetic (seeded N(0,1)*%g, per-rank seed)" % wl["factor"],
+            config=dict(workload=wl["name"], B_per_gpu=B, H_Q=Hq, H_KV=Hkv, N=N, D=D, causal=causal,
+                        window=window, global_batch=B * world, seq_len=N, parallelism=f"(b,kv-group) units, dp{world}",
+                        l2="inputs larger than L2 (Q, dO 512 MiB each); no flush"),
+            fwd=dict(value=round(world * flops_fwd / (ms_fwd * 1e-3) / 1e12, 2), unit="TFLOPS/s",
+                     ms=round(ms_fwd, 3)),
+            roofline=roofline, cpu_baseline=cpu, e2e=e2e, clocks=clocks.summary(),
+            gpu_launches=4 * args.steps, kernel_status=status,
+        )
+        print(json.dumps(line), flush=True)
+
+
+def run_reference(args, wl, world, rank):
+    if rank != 0:
+        return
+    cores = os.cpu_count()
+    rows = cpu_calibrate(wl, args.cpu_seconds)
+    for s in range(args.warmup):
+        cpu_sample_run(wl, max(64, rows // 8), seed=100 + s)
+    times, fl = [], None
+    for s in range(args.steps):
+        dt, fl = cpu_sample_run(wl, rows, seed=s)
+        times.append(dt)
+    t = statistics.mean(times)
+    value = fl / t / 1e12
+    sample = (f"oracle port (numpy fp32, {cores} BLAS threads): fwd+bwd of query head 0, the last {rows} "
+              f"query rows of N={wl['N']} (D={wl['D']}) against all keys per step")
+    line = dict(
+        metric=METRIC, value=round(value, 5), unit="TFLOPS/s", n_gpus=world, steps=args.steps,
+        warmup=args.warmup, ms_per_step=round(t * 1e3, 1), higher_is_better=True, scaling="weak",
+        vs_baseline=None, dtype="f32", data="synthetic", impl="reference",
+        config=dict(workload=wl["name"], B_per_gpu=wl["B"], H_Q=wl["Hq"], H_KV=wl["Hkv"], N=wl["N"], D=wl["D"],
+                    causal=wl["causal"], window=wl["W"], global_batch=wl["B"] * world, seq_len=wl["N"],
+                    parallelism="host cores"),
+        cpu_baseline=dict(value=round(value, 5), unit="TFLOPS/s", cores=cores, kind="port", sample=sample),
+        e2e=dict(value=round(value, 5), unit="TFLOPS/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+    )
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    wl = dict(WORKLOADS[args.workload])
+    if args.seqlen:
+        wl["N"] = args.seqlen
+        wl["name"] = wl["name"].replace("N=16384", f"N={args.seqlen}")
+    world, rank, local = setup_dist()
+    try:
+        if args.impl == "reference":
+            run_reference(args, wl, world, rank)
+        else:
+            run_ours(args, wl, world, rank, local)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

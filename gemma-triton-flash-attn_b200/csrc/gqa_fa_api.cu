@@ -108,6 +108,20 @@ int encode_map(CUtensorMap* m, const TensorDesc& t, int B, int N, int D, int box
   return GQAFA_OK;
 }
 
+// Make the device of `stream` (or the current device for the legacy stream)
+// current on this thread with its primary context bound. Needed because the
+// caller may run on a thread where no context is current yet (for example the
+// autograd engine's worker thread), and the driver calls below (tensor-map
+// encoding) need one.
+int bind_device(cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = (stream != nullptr) ? cudaStreamGetDevice(stream, &dev) : cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(GQAFA_ERR_CUDA, "cannot resolve the stream's device: %s", cudaGetErrorString(e));
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return fail(GQAFA_ERR_CUDA, "cudaSetDevice(%d): %s", dev, cudaGetErrorString(e));
+  return GQAFA_OK;
+}
+
 int* status_ptr() {
   static std::mutex mu;
   static int* ptrs[128] = {};
@@ -229,11 +243,12 @@ int fwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
 template <bool BF16, class CQ, class CK, class CV>
 int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const TensorDesc& v,
              const TensorDesc& o, const TensorDesc& dout, const float* lse, void* dq, const TensorDesc& dqd,
-             void* dk, const TensorDesc& dkd, void* dv, const TensorDesc& dvd, float* delta, cudaStream_t st) {
+             void* dk, const TensorDesc& dkd, void* dv, const TensorDesc& dvd, float* delta, cudaStream_t st,
+             int stages) {
   int* status = status_ptr();
   if (!status) return fail(GQAFA_ERR_CUDA, "cannot resolve the device status word");
   int rc;
-  {  // dQ + delta
+  if (stages & 1) {  // dQ + delta
     CUtensorMap maps[5];
     if ((rc = encode_map(&maps[0], q, pr.B, pr.N, pr.D, CQ::M, BF16))) return rc;
     if ((rc = encode_map(&maps[1], dout, pr.B, pr.N, pr.D, CQ::M, BF16))) return rc;
@@ -255,7 +270,7 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
     p.status = status;
     if ((rc = launch<CQ>(maps, p, st))) return rc;
   }
-  {  // dK
+  if (stages & 2) {  // dK
     CUtensorMap maps[5];
     if ((rc = encode_map(&maps[0], k, pr.B, pr.N, pr.D, CK::M, BF16))) return rc;
     if ((rc = encode_map(&maps[1], v, pr.B, pr.N, pr.D, CK::M, BF16))) return rc;
@@ -269,7 +284,7 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
     p.status = status;
     if ((rc = launch<CK>(maps, p, st))) return rc;
   }
-  {  // dV
+  if (stages & 4) {  // dV
     CUtensorMap maps[5];
     if ((rc = encode_map(&maps[0], k, pr.B, pr.N, pr.D, CV::M, BF16))) return rc;
     if ((rc = encode_map(&maps[2], q, pr.B, pr.N, pr.D, CV::BN, BF16))) return rc;
@@ -308,6 +323,7 @@ extern "C" int gqafa_fwd(const void* q, const long long* q_strides, const void* 
   if (lse != nullptr && reinterpret_cast<uintptr_t>(lse) % 4 != 0)
     return fail(GQAFA_ERR_INVALID, "lse must be 4-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = bind_device(st))) return rc;
   if (pr.D == 256)
     return pr.bf16 ? fwd_impl<true, Fwd256<true>>(pr, qd, kd, vd, o, od, lse, st)
                    : fwd_impl<false, Fwd256<false>>(pr, qd, kd, vd, o, od, lse, st);
@@ -315,7 +331,7 @@ extern "C" int gqafa_fwd(const void* q, const long long* q_strides, const void* 
                  : fwd_impl<false, Fwd512<false>>(pr, qd, kd, vd, o, od, lse, st);
 }
 
-extern "C" int gqafa_bwd(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+static int bwd_entry(int stages, const void* q, const long long* q_strides, const void* k, const long long* k_strides,
                          const void* v, const long long* v_strides, const void* o, const long long* o_strides,
                          const void* dout, const long long* dout_strides, const float* lse, void* dq,
                          const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
@@ -323,6 +339,7 @@ extern "C" int gqafa_bwd(const void* q, const long long* q_strides, const void* 
                          int seqlen, int head_dim, float softmax_scale, int causal, int window, int dtype,
                          void* stream) {
   g_last_error.clear();
+  if (stages <= 0 || stages > 7) return fail(GQAFA_ERR_INVALID, "stage mask %d not in 1..7", stages);
   Problem pr;
   int rc;
   if ((rc = check_problem(batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, window, dtype, &pr)))
@@ -338,15 +355,39 @@ extern "C" int gqafa_bwd(const void* q, const long long* q_strides, const void* 
   if ((rc = check_tensor("dv", dv, dv_strides, batch, heads_kv, seqlen, head_dim, &dvd))) return rc;
   if (lse == nullptr || delta == nullptr) return fail(GQAFA_ERR_INVALID, "lse and delta must be non-null");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = bind_device(st))) return rc;
   if (pr.D == 256)
     return pr.bf16 ? bwd_impl<true, Dq256<true>, Dk256<true>, Dv256<true>>(pr, qd, kd, vd, od, dod, lse, dq, dqd,
-                                                                            dk, dkd, dv, dvd, delta, st)
+                                                                            dk, dkd, dv, dvd, delta, st, stages)
                    : bwd_impl<false, Dq256<false>, Dk256<false>, Dv256<false>>(pr, qd, kd, vd, od, dod, lse, dq,
-                                                                               dqd, dk, dkd, dv, dvd, delta, st);
+                                                                               dqd, dk, dkd, dv, dvd, delta, st, stages);
   return pr.bf16 ? bwd_impl<true, Dq512<true>, Dk512<true>, Dv512<true>>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk,
-                                                                          dkd, dv, dvd, delta, st)
+                                                                          dkd, dv, dvd, delta, st, stages)
                  : bwd_impl<false, Dq512<false>, Dk512<false>, Dv512<false>>(pr, qd, kd, vd, od, dod, lse, dq, dqd,
-                                                                             dk, dkd, dv, dvd, delta, st);
+                                                                             dk, dkd, dv, dvd, delta, st, stages);
+}
+
+
+#define GQAFA_BWD_PARAMS                                                                                      \
+  const void *q, const long long *q_strides, const void *k, const long long *k_strides, const void *v,      \
+      const long long *v_strides, const void *o, const long long *o_strides, const void *dout,              \
+      const long long *dout_strides, const float *lse, void *dq, const long long *dq_strides, void *dk,     \
+      const long long *dk_strides, void *dv, const long long *dv_strides, float *delta, int batch,          \
+      int heads_q, int heads_kv, int seqlen, int head_dim, float softmax_scale, int causal, int window,     \
+      int dtype, void *stream
+#define GQAFA_BWD_ARGS                                                                                        \
+  q, q_strides, k, k_strides, v, v_strides, o, o_strides, dout, dout_strides, lse, dq, dq_strides, dk,      \
+      dk_strides, dv, dv_strides, delta, batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, \
+      window, dtype, stream
+
+extern "C" int gqafa_bwd(GQAFA_BWD_PARAMS) { return bwd_entry(7, GQAFA_BWD_ARGS); }
+
+extern "C" int gqafa_bwd_stage(int stage, GQAFA_BWD_PARAMS) {
+  if (stage < 0 || stage > 2) {
+    g_last_error = "stage must be 0 (dQ + delta), 1 (dK) or 2 (dV)";
+    return GQAFA_ERR_INVALID;
+  }
+  return bwd_entry(1 << stage, GQAFA_BWD_ARGS);
 }
 
 extern "C" int gqafa_supported(int head_dim, int dtype) {

@@ -26,6 +26,7 @@ GQAFA_ERR_CUDA = 3
 EXPORTED_SYMBOLS = (
     "gqafa_fwd",
     "gqafa_bwd",
+    "gqafa_bwd_stage",
     "gqafa_supported",
     "gqafa_last_error",
     "gqafa_device_status",
@@ -65,6 +66,8 @@ def load():
             + [_I, _I, _I, _I, _I, _F, _I, _I, _I, _P]
         )
         lib.gqafa_bwd.restype = _I
+        lib.gqafa_bwd_stage.argtypes = [_I] + lib.gqafa_bwd.argtypes
+        lib.gqafa_bwd_stage.restype = _I
         lib.gqafa_supported.argtypes = [_I, _I]
         lib.gqafa_supported.restype = _I
         lib.gqafa_last_error.argtypes = []

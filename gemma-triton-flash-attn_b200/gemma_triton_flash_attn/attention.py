@@ -192,19 +192,25 @@ def _fwd(q, k, v, causal, window, scale, want_lse):
     return o, lse
 
 
-def _bwd(q, k, v, o, lse, do, causal, window, scale):
+def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None):
+    """Backward launches. `stage` (0 dQ+delta, 1 dK, 2 dV) runs one kernel only,
+    into the buffers of `out` = (dq, dk, dv, delta) (profiling / benchmarks)."""
     lib = _lib.load()
     b, h_q, n, d = q.shape
     h_kv = k.shape[1]
     q, k, v, o = _abi_ready(q), _abi_ready(k), _abi_ready(v), _abi_ready(o)
     do = _abi_ready(do)
-    dq = _abi_ready(torch.empty_like(q))
-    dk = _abi_ready(torch.empty_like(k))
-    dv = _abi_ready(torch.empty_like(v))
-    delta = torch.empty((b, h_q, n), dtype=torch.float32, device=q.device)
+    if out is None:
+        dq = _abi_ready(torch.empty_like(q))
+        dk = _abi_ready(torch.empty_like(k))
+        dv = _abi_ready(torch.empty_like(v))
+        delta = torch.empty((b, h_q, n), dtype=torch.float32, device=q.device)
+    else:
+        dq, dk, dv, delta = out
+    fn = lib.gqafa_bwd if stage is None else (lambda *a: lib.gqafa_bwd_stage(int(stage), *a))
     with _DeviceScope(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        rc = lib.gqafa_bwd(
+        rc = fn(
             q.data_ptr(), _lib.strides_arg(q.stride()),
             k.data_ptr(), _lib.strides_arg(k.stride()),
             v.data_ptr(), _lib.strides_arg(v.stride()),

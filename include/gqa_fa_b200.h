@@ -72,6 +72,20 @@ GQAFA_API int gqafa_bwd(const void* q, const long long* q_strides, const void* k
               int seqlen, int head_dim, float softmax_scale, int causal, int window, int dtype,
               void* stream);
 
+/* One stage of gqafa_bwd, same arguments: stage 0 = dQ with the delta
+ * prologue (replaces the dQ launch, flash_attn/attention.py:1506-1523),
+ * 1 = dK and 2 = dV (together they replace the packed dK/dV launch,
+ * flash_attn/attention.py:1602-1620). Stage 0 must run before 1 (dK reads
+ * delta). For per-kernel timing and profiling; gqafa_bwd runs all three. */
+GQAFA_API int gqafa_bwd_stage(int stage, const void* q, const long long* q_strides, const void* k,
+                              const long long* k_strides, const void* v, const long long* v_strides,
+                              const void* o, const long long* o_strides, const void* dout,
+                              const long long* dout_strides, const float* lse, void* dq,
+                              const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
+                              const long long* dv_strides, float* delta, int batch, int heads_q,
+                              int heads_kv, int seqlen, int head_dim, float softmax_scale, int causal,
+                              int window, int dtype, void* stream);
+
 /* 1 if (head_dim, dtype) has a compiled kernel set, else 0. */
 GQAFA_API int gqafa_supported(int head_dim, int dtype);
 

@@ -54,25 +54,31 @@ def mask_block(q0: int, q1: int, k0: int, k1: int, n: int, causal: bool, window:
     return ok
 
 
-def attention_fwd(q, k, v, causal=False, window=0, scale=None, dtype=np.float32, chunk=512):
-    """Returns (O, LSE). q: (B,Hq,N,D), k/v: (B,Hkv,N,D) arrays of any float type."""
-    b_sz, hq, n, d = q.shape
+def attention_fwd(q, k, v, causal=False, window=0, scale=None, dtype=np.float32, chunk=512, q_offset=0):
+    """Returns (O, LSE). q: (B,Hq,Nq,D), k/v: (B,Hkv,N,D) arrays of any float type.
+
+    The query rows are sequence positions q_offset .. q_offset+Nq-1 (Nq = N and
+    q_offset = 0 for full self-attention; a row subset for bounded samples).
+    """
+    b_sz, hq, n_q, d = q.shape
+    n = k.shape[2]
     hkv = k.shape[1]
     g = hq // hkv
     w = _window(causal, window, n)
     scale = (1.0 / np.sqrt(d)) if scale is None else scale
-    o = np.zeros((b_sz, hq, n, d), dtype=dtype)
-    lse = np.full((b_sz, hq, n), -np.inf, dtype=dtype)
+    o = np.zeros((b_sz, hq, n_q, d), dtype=dtype)
+    lse = np.full((b_sz, hq, n_q), -np.inf, dtype=dtype)
     for b in range(b_sz):
         for h in range(hq):
             kh = k[b, h // g].astype(dtype)
             vh = v[b, h // g].astype(dtype)
-            for q0 in range(0, n, chunk):
-                q1 = min(n, q0 + chunk)
-                k0 = max(0, q0 - w + 1) if w else 0
-                k1 = min(n, q1) if causal else n
+            for q0 in range(0, n_q, chunk):
+                q1 = min(n_q, q0 + chunk)
+                a0, a1 = q0 + q_offset, q1 + q_offset
+                k0 = max(0, a0 - w + 1) if w else 0
+                k1 = min(n, a1) if causal else n
                 s = (q[b, h, q0:q1].astype(dtype) @ kh[k0:k1].T) * dtype(scale)
-                m = mask_block(q0, q1, k0, k1, n, causal, w)
+                m = mask_block(a0, a1, k0, k1, n, causal, w)
                 s = np.where(m, s, -np.inf)
                 mx = s.max(axis=1, keepdims=True)
                 mx = np.where(np.isfinite(mx), mx, 0)
@@ -83,14 +89,17 @@ def attention_fwd(q, k, v, causal=False, window=0, scale=None, dtype=np.float32,
     return o, lse
 
 
-def attention_bwd(q, k, v, o, lse, do, causal=False, window=0, scale=None, dtype=np.float32, chunk=512):
-    """Returns (dQ, dK, dV, delta) given the forward's O and LSE."""
-    b_sz, hq, n, d = q.shape
+def attention_bwd(q, k, v, o, lse, do, causal=False, window=0, scale=None, dtype=np.float32, chunk=512,
+                  q_offset=0):
+    """Returns (dQ, dK, dV, delta) given the forward's O and LSE (query rows as
+    in attention_fwd; dK/dV then hold the contributions of those rows only)."""
+    b_sz, hq, n_q, d = q.shape
+    n = k.shape[2]
     hkv = k.shape[1]
     g = hq // hkv
     w = _window(causal, window, n)
     scale = (1.0 / np.sqrt(d)) if scale is None else scale
-    dq = np.zeros((b_sz, hq, n, d), dtype=dtype)
+    dq = np.zeros((b_sz, hq, n_q, d), dtype=dtype)
     dk = np.zeros((b_sz, hkv, n, d), dtype=dtype)
     dv = np.zeros((b_sz, hkv, n, d), dtype=dtype)
     delta = (do.astype(dtype) * o.astype(dtype)).sum(axis=-1)
@@ -99,14 +108,15 @@ def attention_bwd(q, k, v, o, lse, do, causal=False, window=0, scale=None, dtype
             kv = h // g
             kh = k[b, kv].astype(dtype)
             vh = v[b, kv].astype(dtype)
-            for q0 in range(0, n, chunk):
-                q1 = min(n, q0 + chunk)
-                k0 = max(0, q0 - w + 1) if w else 0
-                k1 = min(n, q1) if causal else n
+            for q0 in range(0, n_q, chunk):
+                q1 = min(n_q, q0 + chunk)
+                a0, a1 = q0 + q_offset, q1 + q_offset
+                k0 = max(0, a0 - w + 1) if w else 0
+                k1 = min(n, a1) if causal else n
                 qh = q[b, h, q0:q1].astype(dtype)
                 doh = do[b, h, q0:q1].astype(dtype)
                 s = (qh @ kh[k0:k1].T) * dtype(scale)
-                m = mask_block(q0, q1, k0, k1, n, causal, w)
+                m = mask_block(a0, a1, k0, k1, n, causal, w)
                 p = np.where(m, np.exp(s - lse[b, h, q0:q1, None].astype(dtype)), 0)
                 dp = doh @ vh[k0:k1].T
                 ds = p * (dp - delta[b, h, q0:q1, None])

@@ -1,0 +1,90 @@
+"""The C-ABI library loads, exports every declared symbol and validates its
+arguments on the host. No GPU needed: every call below fails validation
+before any CUDA work."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from gemma_triton_flash_attn import _lib
+
+HEADER = os.path.join(ROOT, "include", "gqa_fa_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return re.findall(r"GQAFA_API\s+[\w\s\*]+?\b(gqafa_\w+)\s*\(", text)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_symbols()
+    assert set(names) == set(_lib.EXPORTED_SYMBOLS)
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_library_is_in_tree_and_built_for_sm100a():
+    assert os.path.commonpath([_lib.LIB_PATH, ROOT]) == ROOT
+    data = open(_lib.LIB_PATH, "rb").read()
+    assert b"sm_100a" in data
+
+
+def test_supported_and_version():
+    lib = _lib.load()
+    assert lib.gqafa_supported(512, 1) == 1 and lib.gqafa_supported(256, 0) == 1
+    assert lib.gqafa_supported(128, 1) == 0 and lib.gqafa_supported(512, 7) == 0
+    assert "sm_100a" in _lib.version()
+
+
+def _fwd(**over):
+    lib = _lib.load()
+    st = _lib.strides_arg((32 * 64 * 512, 64 * 512, 512, 1))
+    kst = _lib.strides_arg((4 * 64 * 512, 64 * 512, 512, 1))
+    fake = 0x100000  # never dereferenced: validation fails first
+    args = dict(q=fake, qs=st, k=fake, ks=kst, v=fake, vs=kst, o=fake, os=st, lse=None,
+                B=1, Hq=32, Hkv=4, N=64, D=512, scale=0.044, causal=1, window=0, dtype=1)
+    args.update(over)
+    return lib.gqafa_fwd(args["q"], args["qs"], args["k"], args["ks"], args["v"], args["vs"],
+                         args["o"], args["os"], args["lse"], args["B"], args["Hq"], args["Hkv"],
+                         args["N"], args["D"], args["scale"], args["causal"], args["window"],
+                         args["dtype"], None)
+
+
+@pytest.mark.parametrize("over,code,msg", [
+    (dict(Hq=30), _lib.GQAFA_ERR_INVALID, "multiple of H_KV"),
+    (dict(D=128), _lib.GQAFA_ERR_UNSUPPORTED, "head_dim 128"),
+    (dict(dtype=3), _lib.GQAFA_ERR_INVALID, "dtype"),
+    (dict(N=0), _lib.GQAFA_ERR_INVALID, "positive"),
+    (dict(scale=0.0), _lib.GQAFA_ERR_INVALID, "softmax_scale"),
+    (dict(window=-1), _lib.GQAFA_ERR_INVALID, "window"),
+    (dict(q=None), _lib.GQAFA_ERR_INVALID, "null pointer"),
+    (dict(q=0x100008), _lib.GQAFA_ERR_INVALID, "16-byte aligned"),
+    (dict(qs=_lib.strides_arg((32 * 64 * 512, 64 * 512, 1, 64))), _lib.GQAFA_ERR_INVALID, "last (head_dim) stride"),
+    (dict(qs=_lib.strides_arg((32 * 64 * 512, 64 * 512, 516, 1))), _lib.GQAFA_ERR_INVALID, "multiples of 8"),
+])
+def test_fwd_validation(over, code, msg):
+    rc = _fwd(**over)
+    assert rc == code
+    assert msg in _lib.load().gqafa_last_error().decode()
+
+
+def test_check_maps_codes_to_python_exceptions():
+    assert _fwd(D=128) == _lib.GQAFA_ERR_UNSUPPORTED
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.GQAFA_ERR_UNSUPPORTED)
+    assert _fwd(Hq=30) == _lib.GQAFA_ERR_INVALID
+    with pytest.raises(ValueError):
+        _lib.check(_lib.GQAFA_ERR_INVALID)
+
+
+def test_bwd_validation_requires_lse_and_delta():
+    lib = _lib.load()
+    st = _lib.strides_arg((8 * 64 * 256, 64 * 256, 256, 1))
+    f = 0x100000
+    rc = lib.gqafa_bwd(f, st, f, st, f, st, f, st, f, st, None, f, st, f, st, f, st, None,
+                       1, 8, 8, 64, 256, 0.0625, 1, 0, 0, None)
+    assert rc == _lib.GQAFA_ERR_INVALID
+    assert "lse and delta" in lib.gqafa_last_error().decode()

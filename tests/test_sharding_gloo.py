@@ -1,0 +1,109 @@
+"""Multi-rank sharding over (batch, KV-head group) units, run as gloo ranks on
+CPU. The per-unit compute is the numpy oracle standing in for the kernel (test
+only): what is under test is the partitioning and the all-gather reassembly."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gemma_triton_flash_attn.sharding import ShardPlan, sharded_backward, sharded_forward
+from oracle.attention_oracle import attention_bwd, attention_fwd
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def oracle_fwd(q, k, v, causal, slide, scale):
+    o, lse = attention_fwd(q.numpy(), k.numpy(), v.numpy(), causal, slide, scale)
+    return torch.from_numpy(o), torch.from_numpy(lse)
+
+
+def oracle_bwd(q, k, v, o, lse, do, causal, slide, scale):
+    dq, dk, dv, _ = attention_bwd(q.numpy(), k.numpy(), v.numpy(), o.numpy(), lse.numpy(), do.numpy(),
+                                  causal, slide, scale)
+    return torch.from_numpy(dq), torch.from_numpy(dk), torch.from_numpy(dv)
+
+
+@pytest.mark.parametrize("B,Hkv,world", [(1, 4, 2), (4, 2, 8), (3, 5, 4), (1, 1, 3), (2, 3, 2)])
+def test_plan_covers_every_unit_once(B, Hkv, world):
+    seen = []
+    sizes = []
+    for r in range(world):
+        plan = ShardPlan(B, Hkv * 2, Hkv, world, r)
+        u0, u1 = plan.unit_range()
+        sizes.append(u1 - u0)
+        for b, kv0, kv1 in plan.runs():
+            seen += [b * Hkv + kv for kv in range(kv0, kv1)]
+    assert seen == list(range(B * Hkv))
+    assert max(sizes) - min(sizes) <= 1
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(7)
+    B, Hq, Hkv, N, D = 2, 6, 3, 33, 16
+    q = torch.randn(B, Hq, N, D, generator=g)
+    k = torch.randn(B, Hkv, N, D, generator=g)
+    v = torch.randn(B, Hkv, N, D, generator=g)
+    do = torch.randn(B, Hq, N, D, generator=g)
+    return q, k, v, do
+
+
+def _worker(rank, world, port, out_dir):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        q, k, v, do = _inputs()
+        o, lse = sharded_forward(q, k, v, True, 5, None, fwd_fn=oracle_fwd)
+        dq, dk, dv = sharded_backward(q, k, v, o, lse, do, True, 5, None, bwd_fn=oracle_bwd)
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), o=o.numpy(), lse=lse.numpy(), dq=dq.numpy(),
+                 dk=dk.numpy(), dv=dv.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_matches_single_rank(tmp_path, world):
+    port = _free_port()
+    mp.spawn(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+    q, k, v, do = _inputs()
+    o, lse = oracle_fwd(q, k, v, True, 5, None)
+    dq, dk, dv = oracle_bwd(q, k, v, o, lse, do, True, 5, None)
+    for r in range(world):
+        z = np.load(os.path.join(tmp_path, f"r{r}.npz"))
+        for name, ref in (("o", o), ("lse", lse), ("dq", dq), ("dk", dk), ("dv", dv)):
+            np.testing.assert_allclose(z[name], ref.numpy(), rtol=1e-5, atol=1e-5, err_msg=f"rank {r} {name}")
+
+
+def _failing_worker(rank, world, port, out_dir):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    q, k, v, do = _inputs()
+    if rank == 1:
+        # This rank fails on the host before its collective; it never joins.
+        os._exit(3)
+    try:
+        sharded_forward(q, k, v, True, 5, None, fwd_fn=oracle_fwd)
+        open(os.path.join(out_dir, "completed"), "w").close()
+    except Exception as e:  # gloo reports the missing peer instead of hanging
+        open(os.path.join(out_dir, "error"), "w").write(type(e).__name__)
+
+
+def test_rank_failure_surfaces_as_error_not_hang(tmp_path):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert not p.is_alive()
+    assert os.path.exists(os.path.join(tmp_path, "error"))
+    assert not os.path.exists(os.path.join(tmp_path, "completed"))
