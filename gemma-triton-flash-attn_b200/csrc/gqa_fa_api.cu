@@ -390,6 +390,79 @@ extern "C" int gqafa_bwd_stage(int stage, GQAFA_BWD_PARAMS) {
   return bwd_entry(1 << stage, GQAFA_BWD_ARGS);
 }
 
+// ---------------------------------------------------------------------------
+// gqafa_bwd_noalloc: the backward for callers that cannot allocate device
+// memory. Some callers hold nothing but their input and output tensors: a
+// binding that passes only q/k/v/o/dO and the gradient buffers across an FFI,
+// or a serving process whose device memory is fully planned up front and
+// which may not call cudaMalloc (an allocation can also synchronise the
+// device) once it is running. The backward needs one fp32 value per query
+// row (delta = rowsum(dO * O)) between its dQ and dK launches, so this entry
+// point keeps that workspace in a fixed device array instead of asking the
+// caller for it.
+//
+// The array is a file-scope __device__ variable: every GPU that loads this
+// library holds it (4 MiB) until the process exits. Host code cannot use the
+// symbol as a pointer, so the first call on each device resolves its device
+// address with cudaGetSymbolAddress while that device is current, and caches
+// it; make that first call before any CUDA stream capture. All calls share the
+// array and it keeps the last call's contents; nothing in it has to start at
+// zero, because the dQ launch writes every delta row before the dK launch
+// reads it. Two calls whose kernels overlap on the GPU (different streams, no
+// ordering between them) race on the array.
+// ---------------------------------------------------------------------------
+namespace gqafa {
+namespace {
+constexpr long long kNoAllocDeltaRows = 1LL << 20;  // B * H_Q * N, fp32 each: 4 MiB
+static __device__ __align__(256) float g_noalloc_delta[kNoAllocDeltaRows];
+
+float* noalloc_delta_ptr() {
+  static std::mutex mu;
+  static float* ptrs[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) {
+    fail(GQAFA_ERR_CUDA, "cannot resolve the current device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_delta);
+    if (e != cudaSuccess) {
+      fail(GQAFA_ERR_CUDA, "cudaGetSymbolAddress(no-alloc scratch): %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  return ptrs[dev];
+}
+}  // namespace
+}  // namespace gqafa
+
+extern "C" int gqafa_bwd_noalloc(const void* q, const long long* q_strides, const void* k,
+                                 const long long* k_strides, const void* v, const long long* v_strides,
+                                 const void* o, const long long* o_strides, const void* dout,
+                                 const long long* dout_strides, const float* lse, void* dq,
+                                 const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
+                                 const long long* dv_strides, int batch, int heads_q, int heads_kv, int seqlen,
+                                 int head_dim, float softmax_scale, int causal, int window, int dtype,
+                                 void* stream) {
+  g_last_error.clear();
+  const long long rows = (long long)batch * heads_q * seqlen;
+  if (batch > 0 && heads_q > 0 && seqlen > 0 && rows > kNoAllocDeltaRows)
+    return fail(GQAFA_ERR_INVALID,
+                "gqafa_bwd_noalloc: B*H_Q*N = %lld exceeds the fixed scratch of %lld rows; "
+                "use gqafa_bwd with a caller-provided delta buffer",
+                rows, kNoAllocDeltaRows);
+  int rc;
+  if ((rc = bind_device(static_cast<cudaStream_t>(stream)))) return rc;
+  float* delta = noalloc_delta_ptr();
+  if (!delta) return GQAFA_ERR_CUDA;
+  return gqafa_bwd(q, q_strides, k, k_strides, v, v_strides, o, o_strides, dout, dout_strides, lse, dq, dq_strides,
+                   dk, dk_strides, dv, dv_strides, delta, batch, heads_q, heads_kv, seqlen, head_dim,
+                   softmax_scale, causal, window, dtype, stream);
+}
+
 extern "C" int gqafa_supported(int head_dim, int dtype) {
   return (head_dim == 256 || head_dim == 512) && (dtype == GQAFA_DTYPE_FP16 || dtype == GQAFA_DTYPE_BF16);
 }

@@ -27,6 +27,7 @@ EXPORTED_SYMBOLS = (
     "gqafa_fwd",
     "gqafa_bwd",
     "gqafa_bwd_stage",
+    "gqafa_bwd_noalloc",
     "gqafa_supported",
     "gqafa_last_error",
     "gqafa_device_status",
@@ -68,6 +69,11 @@ def load():
         lib.gqafa_bwd.restype = _I
         lib.gqafa_bwd_stage.argtypes = [_I] + lib.gqafa_bwd.argtypes
         lib.gqafa_bwd_stage.restype = _I
+        lib.gqafa_bwd_noalloc.argtypes = (
+            [_P, _S, _P, _S, _P, _S, _P, _S, _P, _S, _P, _P, _S, _P, _S, _P, _S]
+            + [_I, _I, _I, _I, _I, _F, _I, _I, _I, _P]
+        )
+        lib.gqafa_bwd_noalloc.restype = _I
         lib.gqafa_supported.argtypes = [_I, _I]
         lib.gqafa_supported.restype = _I
         lib.gqafa_last_error.argtypes = []

@@ -86,6 +86,24 @@ GQAFA_API int gqafa_bwd_stage(int stage, const void* q, const long long* q_strid
                               int heads_kv, int seqlen, int head_dim, float softmax_scale, int causal,
                               int window, int dtype, void* stream);
 
+/* gqafa_bwd without the delta argument, for callers that cannot allocate
+ * device memory (an FFI binding that only holds its input and output tensors,
+ * or a process whose device memory is planned up front and may not call
+ * cudaMalloc). No counterpart in the reference. The delta workspace lives in
+ * a fixed 4 MiB device array inside the library, which limits B * H_Q * N to
+ * 1,048,576 (larger sizes return GQAFA_ERR_INVALID). The first call on a
+ * device looks up the array's address, so make it before any CUDA stream
+ * capture. All calls share the array: calls whose kernels overlap on the GPU
+ * race on it. Allocates nothing. */
+GQAFA_API int gqafa_bwd_noalloc(const void* q, const long long* q_strides, const void* k,
+                                const long long* k_strides, const void* v, const long long* v_strides,
+                                const void* o, const long long* o_strides, const void* dout,
+                                const long long* dout_strides, const float* lse, void* dq,
+                                const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
+                                const long long* dv_strides, int batch, int heads_q, int heads_kv, int seqlen,
+                                int head_dim, float softmax_scale, int causal, int window, int dtype,
+                                void* stream);
+
 /* 1 if (head_dim, dtype) has a compiled kernel set, else 0. */
 GQAFA_API int gqafa_supported(int head_dim, int dtype);
 
