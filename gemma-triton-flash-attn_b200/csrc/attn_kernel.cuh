@@ -64,6 +64,8 @@ struct Cfg {
   static constexpr int ROLE = ROLE_, M = M_, D = D_, DC = DC_, BN = BN_, NS = NS_;
   static constexpr int NSTAGES = NSTAGES_, YGROUP = YGROUP_;
   static constexpr bool BF16 = BF16_;
+  static constexpr bool PAIR = false;
+  static constexpr int MP = M;  // rows of one grid tile
   static constexpr bool HAS_DP = (ROLE == ROLE_DQ || ROLE == ROLE_DK);
   static constexpr bool ROWS_ARE_Q = (ROLE == ROLE_FWD || ROLE == ROLE_DQ);
   static constexpr bool ATMEM = (M == 128);  // P / dS handed to the MMA through TMEM
@@ -72,11 +74,12 @@ struct Cfg {
   static constexpr int PANELS_Y = DC / 64;
   static constexpr int R_PANEL = M * 128;
   static constexpr int STAGE_BYTES = BN * 128;
+  static constexpr int C_BOX = BN, Y_BOX = BN;  // TMA box rows of the streamed operands
   static constexpr int R_BYTES = PANELS_D * R_PANEL * (HAS_DP ? 2 : 1);
   static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;
   static constexpr int PBUF_ONE = M * BN * 2;
   static constexpr int PBUF_BYTES = ATMEM ? 0 : NS * PBUF_ONE;
-  static constexpr int NBARS = 2 * NSTAGES + 1 + 2 * NS + 1;
+  static constexpr int NBARS = 2 * NSTAGES + 1 + 2 * NS + 2;
   static constexpr int MISC_BYTES = M * 4 + NBARS * 8 + 16;
   static constexpr int SMEM_BYTES = 1024 + R_BYTES + RING_BYTES + PBUF_BYTES + MISC_BYTES;
   // TMEM columns
@@ -140,6 +143,10 @@ __global__ void __launch_bounds__(256, 1)
   auto BAR_SFULL = [&](int s) { return bar0 + 8u * (2 * NST + 1 + s); };
   auto BAR_PREADY = [&](int s) { return bar0 + 8u * (2 * NST + 1 + NS + s); };
   const uint32_t BAR_ACC = bar0 + 8u * (2 * NST + 1 + 2 * NS);
+  // Completes once, after the last accumulate MMA. The epilogue waits on it
+  // rather than on BAR_ACC: with two score buffers BAR_ACC can still be two
+  // phases short of the end, where its parity is indistinguishable.
+  const uint32_t BAR_FINAL = bar0 + 8u * (2 * NST + 2 + 2 * NS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -186,6 +193,7 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(BAR_PREADY(s), 4);
     }
     mbar_init(BAR_ACC, 1);
+    mbar_init(BAR_FINAL, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -319,6 +327,7 @@ __global__ void __launch_bounds__(256, 1)
         ok = issue_acc(i);
         if (ok && i + NS < n_items) ok = issue_scores(i + NS);
       }
+      if (ok) mma_commit(BAR_FINAL);
     }
   } else if (warp >= 4) {
     // ======================= row warps =======================
@@ -538,7 +547,7 @@ __global__ void __launch_bounds__(256, 1)
 
     // ---------------- epilogue ----------------
     if (ok && n_items > 0) {
-      ok = mbar_wait(BAR_ACC, (n_items - 1) & 1u, abort_flag, p.status, ST_TIMEOUT_ACC);
+      ok = mbar_wait(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok && n_items > 0) {

@@ -1,0 +1,449 @@
+// Head_dim-512 backward kernels on CTA pairs (cta_group::2).
+//
+// Same roles and math as attn_kernel.cuh (ROLE_DQ / ROLE_DK / ROLE_DV; the
+// reference launches they replace are listed there), but a row tile of 128
+// rows is shared by the two CTAs of a cluster, 64 rows each:
+//
+//   * every tcgen05.mma is issued by the even CTA (the leader) with
+//     cta_group::2 and M = 128: A comes from each CTA's own 64 rows, B is split
+//     along N between the two CTAs, and each CTA's TMEM receives its 64 rows;
+//   * so each CTA loads only half of every streamed B operand: the score MMAs
+//     read BN/2 key (or query) rows per CTA, the accumulate MMAs 128 of every
+//     256 head_dim columns per CTA;
+//   * the fp32 accumulator of 64 rows x 512 columns takes 256 TMEM columns per
+//     CTA (the 2x2 layout: lanes 0-63 hold the first half of each N range,
+//     lanes 64-127 the second half), which leaves room for double-buffered
+//     score buffers.
+//
+// Synchronisation across the pair: TMA loads of both CTAs complete on the
+// leader's "full" barriers (the leader expects both CTAs' bytes); the
+// leader's tcgen05.commit arrives on the "empty", "scores ready" and
+// "accumulator done" barriers of both CTAs (multicast commit); the row warps
+// of both CTAs arrive on the leader's "P ready" barrier. No TMA multicast is
+// used. Every wait is bounded as in attn_kernel.cuh.
+#pragma once
+#include "attn_kernel.cuh"
+
+namespace gqafa {
+
+template <int ROLE_, int D_, int BN_, int NS_, int NSTAGES_, bool BF16_>
+struct PairCfg {
+  static constexpr int ROLE = ROLE_, D = D_, BN = BN_, NS = NS_, NSTAGES = NSTAGES_;
+  static constexpr bool BF16 = BF16_;
+  static constexpr bool PAIR = true;
+  static constexpr int M = 64;     // rows per CTA
+  static constexpr int MP = 128;   // rows per pair
+  static constexpr int NCHUNK = 1;
+  static constexpr bool HAS_DP = (ROLE == ROLE_DQ || ROLE == ROLE_DK);
+  static constexpr bool ROWS_ARE_Q = (ROLE == ROLE_DQ);
+  static constexpr int PANELS_D = D / 64;
+  static constexpr int R_PANEL = M * 128;
+  static constexpr int R_BYTES = PANELS_D * R_PANEL * (HAS_DP ? 2 : 1);
+  static constexpr int STAGE_BYTES = BN * 128;          // one Y panel (BN rows) or two C panels
+  static constexpr int C_PANEL_BYTES = (BN / 2) * 128;  // BN/2 rows of one 64-column panel
+  static constexpr int C_STAGES = PANELS_D / 2;
+  static constexpr int C_BOX = BN / 2, Y_BOX = BN;
+  static constexpr int NACC = D / 256;                  // N=256 accumulate instructions per k-step
+  static constexpr int Y_STAGES = NACC * 2;             // this CTA's 128 of every 256 columns
+  static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;
+  static constexpr int PBUF_ONE = M * BN * 2;
+  static constexpr int PBUF_BYTES = NS * PBUF_ONE;
+  static constexpr int NBARS = 2 * NSTAGES + 1 + 2 * NS + 2;
+  static constexpr int MISC_BYTES = M * 4 + NBARS * 8 + 16;
+  static constexpr int SMEM_BYTES = 1024 + R_BYTES + RING_BYTES + PBUF_BYTES + MISC_BYTES;
+  static constexpr int ACC_COLS = D / 2;
+  static constexpr int SBUF_COLS = BN / 2;
+  static constexpr uint32_t IDESC_S = make_idesc(MP, BN, BF16, false);
+  static constexpr uint32_t IDESC_Y = make_idesc(MP, 256, BF16, true);
+
+  static_assert(D % 256 == 0, "D");
+  static_assert(BN == 128, "BN");
+  static_assert(ACC_COLS + NS * SBUF_COLS * (HAS_DP ? 2 : 1) <= 512, "TMEM");
+  static_assert(NSTAGES % 2 == 0, "ring groups");
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+  static_assert(ROLE != ROLE_FWD, "backward roles only");
+};
+
+template <class C>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+    attn_pair_kernel(const __grid_constant__ CUtensorMap tmR1, const __grid_constant__ CUtensorMap tmR2,
+                     const __grid_constant__ CUtensorMap tmC1, const __grid_constant__ CUtensorMap tmC2,
+                     const __grid_constant__ CUtensorMap tmY, const KParams p) {
+  constexpr int M = C::M, MP = C::MP, BN = C::BN, NS = C::NS, NST = C::NSTAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sR1 = smem;
+  uint8_t* sR2 = smem + C::PANELS_D * C::R_PANEL;
+  uint8_t* sRing = smem + C::R_BYTES;
+  uint8_t* sP = sRing + C::RING_BYTES;
+  float* sRow = reinterpret_cast<float*>(sP + C::PBUF_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + M);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR_FULL = [&](int s) { return bar0 + 8u * s; };
+  auto BAR_EMPTY = [&](int s) { return bar0 + 8u * (NST + s); };
+  const uint32_t BAR_RFULL = bar0 + 8u * (2 * NST);
+  auto BAR_SFULL = [&](int s) { return bar0 + 8u * (2 * NST + 1 + s); };
+  auto BAR_PREADY = [&](int s) { return bar0 + 8u * (2 * NST + 1 + NS + s); };
+  const uint32_t BAR_ACC = bar0 + 8u * (2 * NST + 1 + 2 * NS);
+  // Completes once, after the last accumulate MMA. The epilogue waits on it
+  // rather than on BAR_ACC: with two score buffers BAR_ACC can still be two
+  // phases short of the end, where its parity is indistinguishable.
+  const uint32_t BAR_FINAL = bar0 + 8u * (2 * NST + 2 + 2 * NS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = (rank == 0);
+
+  // ---- tile decode (per pair; both CTAs see the same items)
+  const int heads = C::ROWS_ARE_Q ? p.Hq : p.Hkv;
+  int idx = blockIdx.x >> 1;
+  const int h = idx % heads;
+  idx /= heads;
+  const int b = idx % p.B;
+  idx /= p.B;
+  const int tile = C::ROWS_ARE_Q ? (p.num_row_tiles - 1 - idx) : idx;
+  const int pr0 = tile * MP;
+  const int r0 = pr0 + M * static_cast<int>(rank);
+  const int N = p.N, G = p.G;
+  const bool swa = p.causal && p.window > 0;
+
+  int jlo, jn, n_items;
+  if constexpr (C::ROWS_ARE_Q) {
+    const int kv_hi = p.causal ? min(N, pr0 + MP) : N;
+    const int kv_lo = swa ? max(0, pr0 - p.window + 1) : 0;
+    jlo = kv_lo / BN;
+    jn = (kv_hi + BN - 1) / BN - jlo;
+    n_items = jn;
+  } else {
+    const int q_lo = p.causal ? pr0 : 0;
+    const int q_hi = swa ? min(N, pr0 + MP - 1 + p.window) : N;
+    jlo = q_lo / BN;
+    jn = (q_hi + BN - 1) / BN - jlo;
+    n_items = G * jn;
+  }
+  auto item_col0 = [&](int i) { return (jlo + (C::ROWS_ARE_Q ? i : i % jn)) * BN; };
+  auto item_headC = [&](int i) { return C::ROWS_ARE_Q ? h / G : h * G + i / jn; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(BAR_FULL(s), 1);
+      mbar_init(BAR_EMPTY(s), 1);
+    }
+    mbar_init(BAR_RFULL, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(BAR_SFULL(s), 1);
+      mbar_init(BAR_PREADY(s), 8);  // 4 row warps in each CTA of the pair
+    }
+    mbar_init(BAR_ACC, 1);
+    mbar_init(BAR_FINAL, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmR1);
+    prefetch_tmap(&tmC1);
+    prefetch_tmap(&tmY);
+    if constexpr (C::HAS_DP) {
+      prefetch_tmap(&tmR2);
+      prefetch_tmap(&tmC2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers are initialised before any cross-CTA arrive
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    // ======================= TMA producer (both CTAs) =======================
+    if (lane == 0) {
+      bool ok = true;
+      if (leader) mbar_arrive_expect_tx(BAR_RFULL, 2 * C::R_BYTES);
+      const uint32_t rfull_l = mapa_shared(BAR_RFULL, 0);
+      for (int pn = 0; pn < C::PANELS_D; ++pn)
+        tma_load_4d_pair(smem_u32(sR1 + pn * C::R_PANEL), &tmR1, rfull_l, 64 * pn, r0, h, b);
+      if constexpr (C::HAS_DP) {
+        for (int pn = 0; pn < C::PANELS_D; ++pn)
+          tma_load_4d_pair(smem_u32(sR2 + pn * C::R_PANEL), &tmR2, rfull_l, 64 * pn, r0, h, b);
+      }
+      uint32_t cnt = 0;
+      // Acquire the next ring stage; the leader announces both CTAs' bytes.
+      auto acquire = [&](int& st) -> bool {
+        st = cnt % NST;
+        const uint32_t ph = (cnt / NST) & 1u;
+        if (!mbar_wait_cluster(BAR_EMPTY(st), ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_RING_EMPTY))
+          return false;
+        if (leader) mbar_arrive_expect_tx(BAR_FULL(st), 2 * C::STAGE_BYTES);
+        ++cnt;
+        return true;
+      };
+      auto load_c = [&](const CUtensorMap* m, int c0, int hc) -> bool {
+        for (int s = 0; s < C::C_STAGES; ++s) {
+          int st;
+          if (!acquire(st)) return false;
+          const uint32_t full_l = mapa_shared(BAR_FULL(st), 0);
+          for (int pp = 0; pp < 2; ++pp)
+            tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES + pp * C::C_PANEL_BYTES), m, full_l,
+                             64 * (2 * s + pp), c0 + static_cast<int>(rank) * (BN / 2), hc, b);
+        }
+        return true;
+      };
+      auto load_scores = [&](int i) -> bool {
+        const int c0 = item_col0(i), hc = item_headC(i);
+        if (!load_c(&tmC1, c0, hc)) return false;
+        if constexpr (C::HAS_DP) {
+          if (!load_c(&tmC2, c0, hc)) return false;
+        }
+        return true;
+      };
+      auto load_y = [&](int i) -> bool {
+        const int c0 = item_col0(i), hc = item_headC(i);
+        for (int g = 0; g < C::NACC; ++g)
+          for (int j = 0; j < 2; ++j) {
+            int st;
+            if (!acquire(st)) return false;
+            tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES), &tmY, mapa_shared(BAR_FULL(st), 0),
+                             64 * (4 * g + 2 * static_cast<int>(rank) + j), c0, hc, b);
+          }
+        return true;
+      };
+      for (int s = 0; s < NS && s < n_items && ok; ++s) ok = load_scores(s);
+      for (int i = 0; i < n_items && ok; ++i) {
+        ok = load_y(i);
+        if (ok && i + NS < n_items) ok = load_scores(i + NS);
+      }
+    }
+  } else if (warp == 1) {
+    // ======================= MMA issuer (leader CTA only) =======================
+    if (leader && lane == 0) {
+      bool ok = mbar_wait_cluster(BAR_RFULL, 0, abort_flag, p.status, ST_TIMEOUT_RESIDENT);
+      tc_fence_after();
+      const uint32_t aR1 = smem_u32(sR1), aR2 = smem_u32(sR2), aRing = smem_u32(sRing), aP = smem_u32(sP);
+      uint32_t cnt = 0;
+      auto scores_from = [&](uint32_t aR, uint32_t d_tmem) -> bool {
+        for (int s = 0; s < C::C_STAGES; ++s) {
+          const int st = cnt % NST;
+          if (!mbar_wait_cluster(BAR_FULL(st), (cnt / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL))
+            return false;
+          tc_fence_after();
+#pragma unroll
+          for (int pp = 0; pp < 2; ++pp) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t ad = sw128_desc(aR + (2 * s + pp) * C::R_PANEL + 32 * k, 16, 1024);
+              const uint64_t bd =
+                  sw128_desc(aRing + st * C::STAGE_BYTES + pp * C::C_PANEL_BYTES + 32 * k, 16, 1024);
+              mma_ss_pair(d_tmem, ad, bd, C::IDESC_S, (s | pp | k) != 0);
+            }
+          }
+          mma_commit_pair(BAR_EMPTY(st));
+          ++cnt;
+        }
+        return true;
+      };
+      auto issue_scores = [&](int i) -> bool {
+        const int sb = i % NS;
+        if (!scores_from(aR1, tbase + C::ACC_COLS + sb * C::SBUF_COLS)) return false;
+        if constexpr (C::HAS_DP) {
+          if (!scores_from(aR2, tbase + C::ACC_COLS + (NS + sb) * C::SBUF_COLS)) return false;
+        }
+        mma_commit_pair(BAR_SFULL(sb));
+        return true;
+      };
+      auto issue_acc = [&](int i) -> bool {
+        const int sb = i % NS;
+        if (!mbar_wait_cluster(BAR_PREADY(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY))
+          return false;
+        for (int j = 0; j < C::Y_STAGES; ++j) {
+          const int st = (cnt + j) % NST;
+          if (!mbar_wait_cluster(BAR_FULL(st), ((cnt + j) / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL))
+            return false;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int t = 0; t < BN / 16; ++t) {
+          const uint64_t ad = sw128_desc(aP + sb * C::PBUF_ONE + (t / 4) * (M * 128) + (t % 4) * 32, 16, 1024);
+#pragma unroll
+          for (int g = 0; g < C::NACC; ++g) {
+            const int st0 = (cnt + 2 * g) % NST;
+            const uint64_t bd = sw128_desc(aRing + st0 * C::STAGE_BYTES + t * 2048, C::STAGE_BYTES, 1024);
+            mma_ss_pair(tbase + g * 128, ad, bd, C::IDESC_Y, (i > 0 || t > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit_pair(BAR_ACC);
+        for (int j = 0; j < C::Y_STAGES; ++j) mma_commit_pair(BAR_EMPTY((cnt + j) % NST));
+        cnt += C::Y_STAGES;
+        return true;
+      };
+      for (int s = 0; s < NS && s < n_items && ok; ++s) ok = issue_scores(s);
+      for (int i = 0; i < n_items && ok; ++i) {
+        ok = issue_acc(i);
+        if (ok && i + NS < n_items) ok = issue_scores(i + NS);
+      }
+      if (ok) mma_commit_pair(BAR_FINAL);
+    }
+  } else if (warp >= 4) {
+    // ======================= row warps (both CTAs) =======================
+    // 2x2 TMEM layout: lane l of quadrant q holds row 32*(q%2)+l, and the
+    // first (q < 2) or second (q >= 2) half of each N range.
+    const int q4 = warp & 3;
+    const int half = q4 >> 1;
+    const int row = 32 * (q4 & 1) + lane;
+    const uint32_t tq = tbase + (static_cast<uint32_t>(q4 * 32) << 16);
+    const float LOG2E = 1.4426950408889634f;
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    float row_lse2 = 0.f, row_delta = 0.f;
+    const long long rowbase_q = (static_cast<long long>(b) * p.Hq + (C::ROWS_ARE_Q ? h : 0)) * N;
+    const uint32_t pready_l0 = mapa_shared(BAR_PREADY(0), 0);
+
+    if constexpr (C::ROLE == ROLE_DQ) {
+      const uint16_t* Og = reinterpret_cast<const uint16_t*>(p.o) + b * p.o_sb + h * p.o_sh;
+      const uint16_t* dOg = reinterpret_cast<const uint16_t*>(p.dout) + b * p.do_sb + h * p.do_sh;
+      for (int r = q4; r < M; r += 4) {
+        const int q = r0 + r;
+        float acc = 0.f;
+        if (q < N) {
+#pragma unroll
+          for (int it = 0; it < C::D / 256; ++it) {
+            const uint4 a = *reinterpret_cast<const uint4*>(Og + q * p.o_sn + it * 256 + lane * 8);
+            const uint4 c = *reinterpret_cast<const uint4*>(dOg + q * p.do_sn + it * 256 + lane * 8);
+            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              acc += unpack_lo<C::BF16>(aw[e]) * unpack_lo<C::BF16>(cw[e]);
+              acc += unpack_hi<C::BF16>(aw[e]) * unpack_hi<C::BF16>(cw[e]);
+            }
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+          sRow[r] = acc;
+          if (q < N) p.delta[rowbase_q + q] = acc;
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      row_delta = sRow[row];
+      row_lse2 = (r0 + row < N) ? p.lse[rowbase_q + r0 + row] * LOG2E : 0.f;
+    }
+
+    for (int i = 0; i < n_items && ok; ++i) {
+      const int sb = i % NS;
+      ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int c0 = item_col0(i);
+      const int cb = c0 + half * (BN / 2);  // first column this thread owns
+      bool need_mask;
+      if constexpr (C::ROWS_ARE_Q) {
+        need_mask = (c0 + BN > N) || (p.causal && c0 + BN - 1 > pr0) || (swa && pr0 + MP - 1 - c0 >= p.window);
+      } else {
+        need_mask = (c0 + BN > N) || (p.causal && pr0 + MP - 1 > c0) || (swa && c0 + BN - 1 - pr0 >= p.window);
+      }
+      const int my_row = r0 + row;
+      const uint32_t s_col = C::ACC_COLS + sb * C::SBUF_COLS;
+      const uint32_t dp_col = C::ACC_COLS + (NS + sb) * C::SBUF_COLS;
+      const int hq = C::ROWS_ARE_Q ? h : item_headC(i);
+      const long long colbase = (static_cast<long long>(b) * p.Hq + hq) * N;
+#pragma unroll 1
+      for (int k = 0; k < C::SBUF_COLS / 32; ++k) {
+        uint32_t rs[32];
+        tmem_ld32(tq + s_col + 32 * k, rs);
+        uint32_t rd[32];
+        if constexpr (C::HAS_DP) tmem_ld32(tq + dp_col + 32 * k, rd);
+        float col_lse2 = 0.f, col_delta = 0.f;
+        if constexpr (!C::ROWS_ARE_Q) {
+          const int qq = cb + 32 * k + lane;
+          if (qq < N) {
+            col_lse2 = p.lse[colbase + qq] * LOG2E;
+            if constexpr (C::HAS_DP) col_delta = p.delta[colbase + qq];
+          }
+        }
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float l2, dl;
+          if constexpr (C::ROWS_ARE_Q) {
+            l2 = row_lse2;
+            dl = row_delta;
+          } else {
+            l2 = __shfl_sync(0xffffffffu, col_lse2, j);
+            dl = C::HAS_DP ? __shfl_sync(0xffffffffu, col_delta, j) : 0.f;
+          }
+          float pv = ex2(__uint_as_float(rs[j]) * sl2 - l2);
+          if (need_mask) {
+            const int col = cb + 32 * k + j;
+            const bool ok_el = C::ROWS_ARE_Q ? attends(my_row, col, N, p.causal, p.window)
+                                             : attends(col, my_row, N, p.causal, p.window);
+            if (!ok_el) pv = 0.f;
+          }
+          if constexpr (C::HAS_DP) {
+            v[j] = pv * (__uint_as_float(rd[j]) - dl);
+          } else {
+            v[j] = pv;
+          }
+        }
+        // K-major SWIZZLE_128B [64 rows x BN] tile: this thread's half is panel `half`.
+        uint8_t* prow = sP + sb * C::PBUF_ONE + half * (M * 128) + row * 128;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int chunk16 = 4 * k + cc;
+          uint4 w;
+          w.x = pack2<C::BF16>(v[8 * cc + 0], v[8 * cc + 1]);
+          w.y = pack2<C::BF16>(v[8 * cc + 2], v[8 * cc + 3]);
+          w.z = pack2<C::BF16>(v[8 * cc + 4], v[8 * cc + 5]);
+          w.w = pack2<C::BF16>(v[8 * cc + 6], v[8 * cc + 7]);
+          *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (row & 7)) * 16)) = w;
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(pready_l0 + 8u * sb);
+    }
+
+    // ---------------- epilogue ----------------
+    if (ok && n_items > 0) {
+      ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok && n_items > 0) {
+      tc_fence_after();
+      const float mul = (C::ROLE == ROLE_DV) ? 1.f : p.scale;
+      const int orow = r0 + row;
+      const long long obase = static_cast<long long>(b) * p.out_sb + static_cast<long long>(h) * p.out_sh +
+                              static_cast<long long>(orow) * p.out_sn;
+#pragma unroll 1
+      for (int g = 0; g < C::NACC; ++g) {
+#pragma unroll 1
+        for (int k = 0; k < 4; ++k) {
+          uint32_t r[32];
+          tmem_ld32(tq + g * 128 + 32 * k, r);
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * mul;
+          if (orow < N) store_row32<C::BF16>(p.out, obase + 256 * g + 128 * half + 32 * k, v);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer has finished reading this CTA's TMEM / smem and arriving on its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, 512);
+  }
+}
+
+}  // namespace gqafa

@@ -19,7 +19,7 @@
 #include <string>
 
 #include "../../include/gqa_fa_b200.h"
-#include "attn_kernel.cuh"
+#include "attn_pair_kernel.cuh"
 
 namespace gqafa {
 
@@ -142,17 +142,27 @@ int launch(const CUtensorMap (&maps)[5], KParams p, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(GQAFA_ERR_CUDA, "cudaGetDevice failed");
   const unsigned long long bit = 1ULL << (dev & 63);
+  const void* kfn;
+  if constexpr (C::PAIR) {
+    kfn = reinterpret_cast<const void*>(&attn_pair_kernel<C>);
+  } else {
+    kfn = reinterpret_cast<const void*>(&attn_kernel<C>);
+  }
   if (!(attr_done_mask.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return fail(GQAFA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_done_mask.fetch_or(bit);
   }
-  p.num_row_tiles = (p.N + C::M - 1) / C::M;
+  p.num_row_tiles = (p.N + C::MP - 1) / C::MP;
   const long long heads = C::ROWS_ARE_Q ? p.Hq : p.Hkv;
-  const long long grid = (long long)p.num_row_tiles * heads * p.B * C::NCHUNK;
+  const long long grid = (long long)p.num_row_tiles * heads * p.B * C::NCHUNK * (C::PAIR ? 2 : 1);
   if (grid <= 0 || grid > 0x7fffffffLL) return fail(GQAFA_ERR_INVALID, "grid size %lld out of range", grid);
-  attn_kernel<C><<<(unsigned)grid, 256, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], p);
+  if constexpr (C::PAIR) {
+    attn_pair_kernel<C><<<(unsigned)grid, 256, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3],
+                                                                         maps[4], p);
+  } else {
+    attn_kernel<C><<<(unsigned)grid, 256, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], p);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(GQAFA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
   return GQAFA_OK;
@@ -164,9 +174,10 @@ template <bool BF16> using Dq256 = Cfg<ROLE_DQ, 128, 256, 256, 128, 1, 6, 2, BF1
 template <bool BF16> using Dk256 = Cfg<ROLE_DK, 128, 256, 256, 128, 1, 6, 2, BF16>;
 template <bool BF16> using Dv256 = Cfg<ROLE_DV, 128, 256, 256, 128, 2, 8, 4, BF16>;
 template <bool BF16> using Fwd512 = Cfg<ROLE_FWD, 128, 512, 256, 128, 2, 6, 2, BF16>;
-template <bool BF16> using Dq512 = Cfg<ROLE_DQ, 64, 512, 512, 64, 2, 8, 4, BF16>;
-template <bool BF16> using Dk512 = Cfg<ROLE_DK, 64, 512, 512, 64, 2, 8, 4, BF16>;
-template <bool BF16> using Dv512 = Cfg<ROLE_DV, 64, 512, 512, 64, 2, 12, 4, BF16>;
+// head_dim 512 backward: CTA pairs, PairCfg<ROLE, D, BN, NS, NSTAGES, BF16>
+template <bool BF16> using Dq512 = PairCfg<ROLE_DQ, 512, 128, 2, 4, BF16>;
+template <bool BF16> using Dk512 = PairCfg<ROLE_DK, 512, 128, 2, 4, BF16>;
+template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 128, 2, 8, BF16>;
 
 struct Problem {
   int B, Hq, Hkv, N, D, causal, window;
@@ -252,9 +263,9 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
     CUtensorMap maps[5];
     if ((rc = encode_map(&maps[0], q, pr.B, pr.N, pr.D, CQ::M, BF16))) return rc;
     if ((rc = encode_map(&maps[1], dout, pr.B, pr.N, pr.D, CQ::M, BF16))) return rc;
-    if ((rc = encode_map(&maps[2], k, pr.B, pr.N, pr.D, CQ::BN, BF16))) return rc;
-    if ((rc = encode_map(&maps[3], v, pr.B, pr.N, pr.D, CQ::BN, BF16))) return rc;
-    maps[4] = maps[2];
+    if ((rc = encode_map(&maps[2], k, pr.B, pr.N, pr.D, CQ::C_BOX, BF16))) return rc;
+    if ((rc = encode_map(&maps[3], v, pr.B, pr.N, pr.D, CQ::C_BOX, BF16))) return rc;
+    if ((rc = encode_map(&maps[4], k, pr.B, pr.N, pr.D, CQ::Y_BOX, BF16))) return rc;
     KParams p = base_params(pr);
     set_out(p, dq, dqd);
     p.lse = const_cast<float*>(lse);
@@ -274,9 +285,9 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
     CUtensorMap maps[5];
     if ((rc = encode_map(&maps[0], k, pr.B, pr.N, pr.D, CK::M, BF16))) return rc;
     if ((rc = encode_map(&maps[1], v, pr.B, pr.N, pr.D, CK::M, BF16))) return rc;
-    if ((rc = encode_map(&maps[2], q, pr.B, pr.N, pr.D, CK::BN, BF16))) return rc;
-    if ((rc = encode_map(&maps[3], dout, pr.B, pr.N, pr.D, CK::BN, BF16))) return rc;
-    maps[4] = maps[2];
+    if ((rc = encode_map(&maps[2], q, pr.B, pr.N, pr.D, CK::C_BOX, BF16))) return rc;
+    if ((rc = encode_map(&maps[3], dout, pr.B, pr.N, pr.D, CK::C_BOX, BF16))) return rc;
+    if ((rc = encode_map(&maps[4], q, pr.B, pr.N, pr.D, CK::Y_BOX, BF16))) return rc;
     KParams p = base_params(pr);
     set_out(p, dk, dkd);
     p.lse = const_cast<float*>(lse);
@@ -287,8 +298,8 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
   if (stages & 4) {  // dV
     CUtensorMap maps[5];
     if ((rc = encode_map(&maps[0], k, pr.B, pr.N, pr.D, CV::M, BF16))) return rc;
-    if ((rc = encode_map(&maps[2], q, pr.B, pr.N, pr.D, CV::BN, BF16))) return rc;
-    if ((rc = encode_map(&maps[4], dout, pr.B, pr.N, pr.D, CV::BN, BF16))) return rc;
+    if ((rc = encode_map(&maps[2], q, pr.B, pr.N, pr.D, CV::C_BOX, BF16))) return rc;
+    if ((rc = encode_map(&maps[4], dout, pr.B, pr.N, pr.D, CV::Y_BOX, BF16))) return rc;
     maps[1] = maps[0];
     maps[3] = maps[2];
     KParams p = base_params(pr);

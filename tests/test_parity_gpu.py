@@ -116,6 +116,8 @@ for D in (256, 512):
         (1, 4, 1, 80, D, False, 16),      # window ignored without causal
         (3, 16, 1, 70, D, True, 0),       # GQA 16:1, B=3
         (2, 8, 8, 150, D, True, 40),      # MHA with window
+        (2, 4, 2, 200, D, True, 0),       # last tile partly past N with two items only:
+        (1, 2, 1, 193, D, False, 0),      # exposed an early epilogue (accumulator not yet final)
     ]
 
 
@@ -240,3 +242,15 @@ def test_full_size_config3_swa_properties():
     dv_sum = dv.float().sum(2)
     do_sum = do.float().view(B, Hkv, G, N, D).sum((2, 3))
     assert ((dv_sum - do_sum).norm() / do_sum.norm()).item() < 2e-3
+
+
+def test_short_tiles_repeated():
+    """Tiles with one or two column items finish their elementwise work
+    quickly; the epilogue must still wait for the last accumulate MMA. Run the
+    shapes that exposed an early read several times."""
+    for rep in range(5):
+        for (B, Hq, Hkv, N, D, causal) in ((2, 4, 2, 200, 512, True), (1, 2, 1, 193, 512, False),
+                                           (1, 4, 2, 130, 256, True), (2, 2, 1, 129, 512, True)):
+            q, k, v, do = make_inputs(B, Hq, Hkv, N, D, torch.bfloat16, 0.5, seed=rep, device=DEV)
+            ref = torch_ref(q, k, v, do, causal, 0)
+            check_all(run_both(q, k, v, do, causal, 0), ref, tag=f"rep{rep} N{N} D{D}")
