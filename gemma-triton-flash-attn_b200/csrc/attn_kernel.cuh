@@ -57,6 +57,23 @@ struct KParams {
   const void* dout;
   long long do_sb, do_sh, do_sn;
   int* status;
+  // Optional diagnostics: when non-null, each CTA adds the cycles its roles
+  // spend waiting (see WaitCounter) into these counters. Null on the hot path.
+  unsigned long long* prof;
+};
+
+// Indices of the wait-cycle diagnostics counters.
+enum WaitCounter : int {
+  WC_PRODUCER_EMPTY = 0,  // producer waiting for a free ring stage
+  WC_MMA_FULL_SCORES = 1, // MMA issuer waiting for score operands to land
+  WC_MMA_FULL_Y = 2,      // MMA issuer waiting for accumulate operands to land
+  WC_MMA_PREADY = 3,      // MMA issuer waiting for the row warps' P / dS
+  WC_ROW_SFULL = 4,       // row warp (lane 0 of warp 4) waiting for scores
+  WC_ROW_WORK = 5,        // row warp elementwise work per item
+  WC_ROW_EPILOGUE = 6,    // row warp waiting for the final MMA + storing
+  WC_CTA_TOTAL = 7,       // whole CTA lifetime (thread 0)
+  WC_CTAS = 8,            // number of CTAs that reported
+  WC_NUM = 9
 };
 
 template <int ROLE_, int M_, int D_, int DC_, int BN_, int NS_, int NSTAGES_, int YGROUP_, bool BF16_>
@@ -99,10 +116,34 @@ struct Cfg {
   static_assert(M == 128 ? (BN % 16 == 0) : (BN % 8 == 0), "N shape");
 };
 
-__device__ __forceinline__ bool attends(int q, int kv, int N, int causal, int window) {
-  if (q >= N || kv >= N) return false;
-  if (!causal) return true;
-  return kv <= q && (window == 0 || q - kv < window);
+// The columns a row attends form one interval [lo, hi) of absolute indices:
+// for a query row q, keys max(0, q-W+1) .. min(q, N-1) (causal) or 0 .. N-1;
+// for a key row k, queries k .. min(k+W-1, N-1) (causal) or 0 .. N-1. Masking
+// is then one unsigned compare per element (an element test inside the
+// unrolled loops costs far more).
+__device__ __forceinline__ void attended_interval(bool row_is_query, int row, int N, int causal, int window,
+                                                  int& lo, int& hi) {
+  if (row >= N) {
+    lo = 0;
+    hi = 0;
+    return;
+  }
+  if (!causal) {
+    lo = 0;
+    hi = N;
+  } else if (row_is_query) {
+    lo = window > 0 ? max(0, row - window + 1) : 0;
+    hi = row + 1;
+  } else {
+    lo = row;
+    hi = window > 0 ? min(N, row + window) : N;
+  }
+}
+
+// Number of in-range columns for relative index test: keep iff
+// (unsigned)(c - lo_rel) < span.
+__device__ __forceinline__ unsigned span_of(int lo_rel, int hi_rel) {
+  return hi_rel > lo_rel ? static_cast<unsigned>(hi_rel - lo_rel) : 0u;
 }
 
 template <bool BF16>
@@ -398,12 +439,11 @@ __global__ void __launch_bounds__(256, 1)
         need_mask = (c0 + BN > N) || (p.causal && r0 + M - 1 > c0) ||
                     (swa && c0 + BN - 1 - r0 >= p.window);
       }
-      const int my_q = C::ROWS_ARE_Q ? (r0 + srow) : 0;
-      const int my_kv = C::ROWS_ARE_Q ? 0 : (r0 + srow);
-      auto valid = [&](int c) {
-        return C::ROWS_ARE_Q ? attends(my_q, c0 + c, N, p.causal, p.window)
-                             : attends(c0 + c, my_kv, N, p.causal, p.window);
-      };
+      int lo_abs, hi_abs;
+      attended_interval(C::ROWS_ARE_Q, r0 + srow, N, p.causal, p.window, lo_abs, hi_abs);
+      const int lo_rel = lo_abs - c0;
+      const unsigned span = span_of(lo_rel, hi_abs - c0);
+      auto valid = [&](int c) { return static_cast<unsigned>(c - lo_rel) < span; };
 
       if constexpr (C::ROLE == ROLE_FWD) {
         float s[BN];
@@ -505,7 +545,7 @@ __global__ void __launch_bounds__(256, 1)
               dl = C::HAS_DP ? __shfl_sync(0xffffffffu, col_delta, j) : 0.f;
             }
             float pv = ex2(__uint_as_float(rs[j]) * sl2 - l2);
-            if (need_mask && !valid(32 * k + j)) pv = 0.f;
+            pv = valid(32 * k + j) ? pv : 0.f;
             if constexpr (C::HAS_DP) {
               v[j] = pv * (__uint_as_float(rd[j]) - dl);
             } else {

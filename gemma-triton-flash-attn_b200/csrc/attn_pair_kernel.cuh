@@ -95,6 +95,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
+  const bool prof = (p.prof != nullptr);
+  unsigned long long wc[WC_NUM] = {};
+  const long long t_start = prof ? clock64() : 0;
+  auto tick = [&]() -> long long { return prof ? clock64() : 0; };
+  auto tock = [&](int k, long long t0) {
+    if (prof) wc[k] += static_cast<unsigned long long>(clock64() - t0);
+  };
   const bool leader = (rank == 0);
 
   // ---- tile decode (per pair; both CTAs see the same items)
@@ -178,8 +185,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       auto acquire = [&](int& st) -> bool {
         st = cnt % NST;
         const uint32_t ph = (cnt / NST) & 1u;
-        if (!mbar_wait_cluster(BAR_EMPTY(st), ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_RING_EMPTY))
-          return false;
+        const long long t0 = tick();
+        const bool got = mbar_wait_cluster(BAR_EMPTY(st), ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_RING_EMPTY);
+        tock(WC_PRODUCER_EMPTY, t0);
+        if (!got) return false;
         if (leader) mbar_arrive_expect_tx(BAR_FULL(st), 2 * C::STAGE_BYTES);
         ++cnt;
         return true;
@@ -227,19 +236,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       tc_fence_after();
       const uint32_t aR1 = smem_u32(sR1), aR2 = smem_u32(sR2), aRing = smem_u32(sRing), aP = smem_u32(sP);
       uint32_t cnt = 0;
-      auto scores_from = [&](uint32_t aR, uint32_t d_tmem) -> bool {
+      // Descriptors are built once; per instruction only the start-address
+      // field changes (byte offset >> 4 added to the low bits). Keeping the
+      // issuing thread's work per MMA to a few integer adds matters: a 128-row
+      // pair MMA with N=128 occupies the tensor pipe for only ~32 cycles.
+      const uint64_t dR1 = sw128_desc(aR1, 16, 1024), dR2 = sw128_desc(aR2, 16, 1024);
+      const uint64_t dRingK = sw128_desc(aRing, 16, 1024);
+      const uint64_t dRingMN = sw128_desc(aRing, C::STAGE_BYTES, 1024);
+      const uint64_t dP = sw128_desc(aP, 16, 1024);
+      auto scores_from = [&](uint64_t dR, uint32_t d_tmem) -> bool {
+#pragma unroll
         for (int s = 0; s < C::C_STAGES; ++s) {
           const int st = cnt % NST;
-          if (!mbar_wait_cluster(BAR_FULL(st), (cnt / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL))
-            return false;
+          const long long t0 = tick();
+          const bool got = mbar_wait_cluster(BAR_FULL(st), (cnt / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL);
+          tock(WC_MMA_FULL_SCORES, t0);
+          if (!got) return false;
           tc_fence_after();
+          const uint64_t bst = dRingK + static_cast<uint64_t>((st * C::STAGE_BYTES) >> 4);
 #pragma unroll
           for (int pp = 0; pp < 2; ++pp) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              const uint64_t ad = sw128_desc(aR + (2 * s + pp) * C::R_PANEL + 32 * k, 16, 1024);
-              const uint64_t bd =
-                  sw128_desc(aRing + st * C::STAGE_BYTES + pp * C::C_PANEL_BYTES + 32 * k, 16, 1024);
+              const uint64_t ad = dR + static_cast<uint64_t>(((2 * s + pp) * C::R_PANEL + 32 * k) >> 4);
+              const uint64_t bd = bst + static_cast<uint64_t>((pp * C::C_PANEL_BYTES + 32 * k) >> 4);
               mma_ss_pair(d_tmem, ad, bd, C::IDESC_S, (s | pp | k) != 0);
             }
           }
@@ -250,32 +270,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       };
       auto issue_scores = [&](int i) -> bool {
         const int sb = i % NS;
-        if (!scores_from(aR1, tbase + C::ACC_COLS + sb * C::SBUF_COLS)) return false;
+        if (!scores_from(dR1, tbase + C::ACC_COLS + sb * C::SBUF_COLS)) return false;
         if constexpr (C::HAS_DP) {
-          if (!scores_from(aR2, tbase + C::ACC_COLS + (NS + sb) * C::SBUF_COLS)) return false;
+          if (!scores_from(dR2, tbase + C::ACC_COLS + (NS + sb) * C::SBUF_COLS)) return false;
         }
         mma_commit_pair(BAR_SFULL(sb));
         return true;
       };
       auto issue_acc = [&](int i) -> bool {
         const int sb = i % NS;
+        long long t0 = tick();
         if (!mbar_wait_cluster(BAR_PREADY(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY))
           return false;
+        tock(WC_MMA_PREADY, t0);
+        t0 = tick();
         for (int j = 0; j < C::Y_STAGES; ++j) {
           const int st = (cnt + j) % NST;
           if (!mbar_wait_cluster(BAR_FULL(st), ((cnt + j) / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL))
             return false;
         }
+        tock(WC_MMA_FULL_Y, t0);
         tc_fence_after();
-#pragma unroll 1
-        for (int t = 0; t < BN / 16; ++t) {
-          const uint64_t ad = sw128_desc(aP + sb * C::PBUF_ONE + (t / 4) * (M * 128) + (t % 4) * 32, 16, 1024);
+        const uint64_t pb = dP + static_cast<uint64_t>((sb * C::PBUF_ONE) >> 4);
+        uint64_t yb[C::NACC];
 #pragma unroll
-          for (int g = 0; g < C::NACC; ++g) {
-            const int st0 = (cnt + 2 * g) % NST;
-            const uint64_t bd = sw128_desc(aRing + st0 * C::STAGE_BYTES + t * 2048, C::STAGE_BYTES, 1024);
-            mma_ss_pair(tbase + g * 128, ad, bd, C::IDESC_Y, (i > 0 || t > 0) ? 1u : 0u);
-          }
+        for (int g = 0; g < C::NACC; ++g)
+          yb[g] = dRingMN + static_cast<uint64_t>((((cnt + 2 * g) % NST) * C::STAGE_BYTES) >> 4);
+        const uint32_t acc0 = (i > 0) ? 1u : 0u;
+#pragma unroll
+        for (int t = 0; t < BN / 16; ++t) {
+          const uint64_t ad = pb + static_cast<uint64_t>(((t / 4) * (M * 128) + (t % 4) * 32) >> 4);
+#pragma unroll
+          for (int g = 0; g < C::NACC; ++g)
+            mma_ss_pair(tbase + g * 128, ad, yb[g] + static_cast<uint64_t>((t * 2048) >> 4), C::IDESC_Y,
+                        t > 0 ? 1u : acc0);
         }
         mma_commit_pair(BAR_ACC);
         for (int j = 0; j < C::Y_STAGES; ++j) mma_commit_pair(BAR_EMPTY((cnt + j) % NST));
@@ -335,39 +363,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       row_lse2 = (r0 + row < N) ? p.lse[rowbase_q + r0 + row] * LOG2E : 0.f;
     }
 
+    constexpr int KCH = C::SBUF_COLS / 32;  // 32-column chunks this thread owns per item
     for (int i = 0; i < n_items && ok; ++i) {
       const int sb = i % NS;
+      const int c0 = item_col0(i);
+      const int cb = c0 + half * (BN / 2);  // first column this thread owns
+      // Per-column softmax statistics (DK / DV), fetched before waiting so the
+      // global-load latency overlaps the MMAs.
+      float col_lse2[KCH], col_delta[KCH];
+      if constexpr (!C::ROWS_ARE_Q) {
+        const int hq = item_headC(i);
+        const long long colbase = (static_cast<long long>(b) * p.Hq + hq) * N;
+#pragma unroll
+        for (int k = 0; k < KCH; ++k) {
+          const int qq = cb + 32 * k + lane;
+          col_lse2[k] = (qq < N) ? p.lse[colbase + qq] * LOG2E : 0.f;
+          col_delta[k] = (C::HAS_DP && qq < N) ? p.delta[colbase + qq] : 0.f;
+        }
+      }
+      const long long t_w = tick();
       ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
+      tock(WC_ROW_SFULL, t_w);
+      const long long t_work = tick();
       tc_fence_after();
-      const int c0 = item_col0(i);
-      const int cb = c0 + half * (BN / 2);  // first column this thread owns
-      bool need_mask;
-      if constexpr (C::ROWS_ARE_Q) {
-        need_mask = (c0 + BN > N) || (p.causal && c0 + BN - 1 > pr0) || (swa && pr0 + MP - 1 - c0 >= p.window);
-      } else {
-        need_mask = (c0 + BN > N) || (p.causal && pr0 + MP - 1 > c0) || (swa && c0 + BN - 1 - pr0 >= p.window);
-      }
-      const int my_row = r0 + row;
+      int lo_abs, hi_abs;
+      attended_interval(C::ROWS_ARE_Q, r0 + row, N, p.causal, p.window, lo_abs, hi_abs);
+      const int lo_rel = lo_abs - cb;
+      const unsigned span = span_of(lo_rel, hi_abs - cb);
       const uint32_t s_col = C::ACC_COLS + sb * C::SBUF_COLS;
       const uint32_t dp_col = C::ACC_COLS + (NS + sb) * C::SBUF_COLS;
-      const int hq = C::ROWS_ARE_Q ? h : item_headC(i);
-      const long long colbase = (static_cast<long long>(b) * p.Hq + hq) * N;
-#pragma unroll 1
-      for (int k = 0; k < C::SBUF_COLS / 32; ++k) {
-        uint32_t rs[32];
-        tmem_ld32(tq + s_col + 32 * k, rs);
-        uint32_t rd[32];
-        if constexpr (C::HAS_DP) tmem_ld32(tq + dp_col + 32 * k, rd);
-        float col_lse2 = 0.f, col_delta = 0.f;
-        if constexpr (!C::ROWS_ARE_Q) {
-          const int qq = cb + 32 * k + lane;
-          if (qq < N) {
-            col_lse2 = p.lse[colbase + qq] * LOG2E;
-            if constexpr (C::HAS_DP) col_delta = p.delta[colbase + qq];
-          }
-        }
+      uint32_t rs[KCH][32], rd[KCH][32];
+#pragma unroll
+      for (int k = 0; k < KCH; ++k) {
+        tmem_ld32_async(tq + s_col + 32 * k, rs[k]);
+        if constexpr (C::HAS_DP) tmem_ld32_async(tq + dp_col + 32 * k, rd[k]);
+      }
+#pragma unroll
+      for (int k = 0; k < KCH; ++k) {
+        tmem_ld_wait32(rs[k]);
+        if constexpr (C::HAS_DP) tmem_ld_wait32(rd[k]);
+      }
+#pragma unroll
+      for (int k = 0; k < KCH; ++k) {
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -376,18 +415,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             l2 = row_lse2;
             dl = row_delta;
           } else {
-            l2 = __shfl_sync(0xffffffffu, col_lse2, j);
-            dl = C::HAS_DP ? __shfl_sync(0xffffffffu, col_delta, j) : 0.f;
+            l2 = __shfl_sync(0xffffffffu, col_lse2[k], j);
+            dl = C::HAS_DP ? __shfl_sync(0xffffffffu, col_delta[k], j) : 0.f;
           }
-          float pv = ex2(__uint_as_float(rs[j]) * sl2 - l2);
-          if (need_mask) {
-            const int col = cb + 32 * k + j;
-            const bool ok_el = C::ROWS_ARE_Q ? attends(my_row, col, N, p.causal, p.window)
-                                             : attends(col, my_row, N, p.causal, p.window);
-            if (!ok_el) pv = 0.f;
-          }
+          float pv = ex2(__uint_as_float(rs[k][j]) * sl2 - l2);
+          pv = (static_cast<unsigned>(32 * k + j - lo_rel) < span) ? pv : 0.f;
           if constexpr (C::HAS_DP) {
-            v[j] = pv * (__uint_as_float(rd[j]) - dl);
+            v[j] = pv * (__uint_as_float(rd[k][j]) - dl);
           } else {
             v[j] = pv;
           }
@@ -409,9 +443,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(pready_l0 + 8u * sb);
+      tock(WC_ROW_WORK, t_work);
     }
 
     // ---------------- epilogue ----------------
+    const long long t_epi = tick();
     if (ok && n_items > 0) {
       ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
       ok = __all_sync(0xffffffffu, ok);
@@ -434,6 +470,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           if (orow < N) store_row32<C::BF16>(p.out, obase + 256 * g + 128 * half + 32 * k, v);
         }
       }
+    }
+    tock(WC_ROW_EPILOGUE, t_epi);
+  }
+
+  if (prof) {
+    // one reporter per role: producer lane 0, MMA lane 0 (leader), warp 4 lane 0, thread 0
+    const bool reporter = (lane == 0 && (warp == 0 || warp == 1 || warp == 4));
+    if (reporter) {
+      for (int k = 0; k < WC_CTA_TOTAL; ++k)
+        if (wc[k]) atomicAdd(p.prof + k, wc[k]);
+    }
+    if (threadIdx.x == 0) {
+      atomicAdd(p.prof + WC_CTA_TOTAL, static_cast<unsigned long long>(clock64() - t_start));
+      atomicAdd(p.prof + WC_CTAS, 1ULL);
     }
   }
 

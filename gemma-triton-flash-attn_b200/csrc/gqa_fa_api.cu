@@ -122,6 +122,9 @@ int bind_device(cudaStream_t stream) {
   return GQAFA_OK;
 }
 
+// Diagnostics buffer (WC_NUM counters) set by gqafa_set_wait_counters; null = off.
+std::atomic<unsigned long long*> g_prof_buffer{nullptr};
+
 int* status_ptr() {
   static std::mutex mu;
   static int* ptrs[128] = {};
@@ -154,6 +157,7 @@ int launch(const CUtensorMap (&maps)[5], KParams p, cudaStream_t stream) {
     attr_done_mask.fetch_or(bit);
   }
   p.num_row_tiles = (p.N + C::MP - 1) / C::MP;
+  p.prof = g_prof_buffer.load(std::memory_order_relaxed);
   const long long heads = C::ROWS_ARE_Q ? p.Hq : p.Hkv;
   const long long grid = (long long)p.num_row_tiles * heads * p.B * C::NCHUNK * (C::PAIR ? 2 : 1);
   if (grid <= 0 || grid > 0x7fffffffLL) return fail(GQAFA_ERR_INVALID, "grid size %lld out of range", grid);
@@ -476,6 +480,11 @@ extern "C" int gqafa_bwd_noalloc(const void* q, const long long* q_strides, cons
 
 extern "C" int gqafa_supported(int head_dim, int dtype) {
   return (head_dim == 256 || head_dim == 512) && (dtype == GQAFA_DTYPE_FP16 || dtype == GQAFA_DTYPE_BF16);
+}
+
+extern "C" int gqafa_set_wait_counters(void* device_counters) {
+  g_prof_buffer.store(static_cast<unsigned long long*>(device_counters));
+  return GQAFA_OK;
 }
 
 extern "C" const char* gqafa_last_error(void) { return g_last_error.c_str(); }

@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "gqafa_last_error",
     "gqafa_device_status",
     "gqafa_version",
+    "gqafa_set_wait_counters",
 )
 
 _lock = threading.Lock()
@@ -80,6 +81,8 @@ def load():
         lib.gqafa_last_error.restype = ctypes.c_char_p
         lib.gqafa_device_status.argtypes = [_I, _I]
         lib.gqafa_device_status.restype = _I
+        lib.gqafa_set_wait_counters.argtypes = [_P]
+        lib.gqafa_set_wait_counters.restype = _I
         lib.gqafa_version.argtypes = []
         lib.gqafa_version.restype = ctypes.c_char_p
         _lib = lib

@@ -116,6 +116,14 @@ GQAFA_API const char* gqafa_last_error(void);
  * error. Not for the hot path. */
 GQAFA_API int gqafa_device_status(int device, int reset);
 
+/* Diagnostics, not for the hot path: point the kernels at a device buffer of
+ * 9 zeroed unsigned 64-bit counters (NULL turns it off). Kernels that support
+ * it (the head_dim-512 backward) then add the cycles each role spends waiting:
+ * [0] producer on free ring stages, [1] MMA issuer on score operands, [2] on
+ * accumulate operands, [3] on the row warps, [4] row warps on scores, [5] row
+ * warps' elementwise work, [6] epilogue, [7] CTA lifetime, [8] CTA count. */
+GQAFA_API int gqafa_set_wait_counters(void* device_counters);
+
 /* Library version string. */
 GQAFA_API const char* gqafa_version(void);
 
