@@ -47,6 +47,9 @@ WORKLOADS = {
                  B=1, Hq=32, Hkv=4, N=16384, D=512, causal=True, W=0, dtype=torch.bfloat16, factor=0.5),
     "cfg3": dict(name="MoE sliding layer: GQA 16/8, D=256, causal SWA W=1024, N=16384, fp16, fwd+bwd",
                  B=1, Hq=16, Hkv=8, N=16384, D=256, causal=True, W=1024, dtype=torch.float16, factor=1.0),
+    "cfg5": dict(name="config 5: random-init Gemma-4-E2B-shaped decoder (35 layers: 7 global D=512 32/4, "
+                      "28 sliding W=512 D=256 16/8), forward through hf_integration, N=16384, bf16",
+                 B=1, Hq=32, Hkv=4, N=16384, D=512, causal=True, W=0, dtype=torch.bfloat16, factor=1.0),
     "cfg4": dict(name="MoE global layer: GQA 16/2, D=512, causal, N=16384, bf16, fwd+bwd (B=4 total)",
                  B=4, Hq=16, Hkv=2, N=16384, D=512, causal=True, W=0, dtype=torch.bfloat16, factor=1.0),
 }
@@ -371,6 +374,54 @@ def run_ours(args, wl, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_decoder(args, wl, world, rank, local):
+    """Config 5: one sequence per GPU (weak scaling), forward tokens/s through
+    register_triton_attention() + the synthetic decoder."""
+    from gemma_triton_flash_attn import register_triton_attention
+    from gemma_triton_flash_attn.flops import attn_flops
+    from gemma_triton_flash_attn.gemma4_synthetic import Gemma4SyntheticConfig, Gemma4SyntheticDecoder
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(device)
+    register_triton_attention()
+    cfg = Gemma4SyntheticConfig()
+    model = Gemma4SyntheticDecoder(cfg).to(device=device, dtype=torch.bfloat16).init_weights(seed=0)
+    N = wl["N"]
+    g = torch.Generator().manual_seed(1000 + rank)
+    ids_h = torch.randint(0, cfg.vocab_size, (1, N), generator=g).pin_memory()
+    ids = torch.empty_like(ids_h, device=device)
+    out_h = torch.empty((1,), dtype=torch.int64).pin_memory()
+
+    def step():
+        ids.copy_(ids_h, non_blocking=True)
+        with torch.no_grad():
+            logits = model(ids)
+        out_h.copy_(logits[0, -1].argmax().view(1), non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    with ClockSampler([uuid if uuid.startswith("GPU-") else "GPU-" + uuid]) as clocks:
+        ms = max_over_ranks(time_loop(step, args.steps, stream), world, device)
+    n_glob = sum(cfg.is_global(i) for i in range(cfg.num_layers))
+    attn_fl = n_glob * attn_flops(1, cfg.global_heads, N, cfg.global_head_dim, True) + \
+        (cfg.num_layers - n_glob) * attn_flops(1, cfg.local_heads, N, cfg.local_head_dim, True, cfg.sliding_window)
+    if rank == 0:
+        line = dict(metric="config-5 decoder forward tokens/s (attention through hf_integration)",
+                    value=round(world * N / (ms * 1e-3), 1), unit="tokens/s", n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=round(ms, 3), higher_is_better=True, scaling="weak",
+                    vs_baseline=None, dtype="bf16", data="synthetic (seeded uniform token ids, random-init weights)",
+                    config=dict(workload=wl["name"], global_batch=world, seq_len=N, parallelism=f"one sequence per GPU, dp{world}"),
+                    attention_tflops_in_step=round(attn_fl / (ms * 1e-3) / 1e12, 1),
+                    e2e=dict(value=round(world * N / (ms * 1e-3), 1), unit="tokens/s", h2d_bytes_per_step=ids_h.numel() * 8,
+                             d2h_bytes_per_step=8),
+                    clocks=clocks.summary(), gpu_launches=35 * args.steps)
+        print(json.dumps(line), flush=True)
+
+
 def run_reference(args, wl, world, rank):
     if rank != 0:
         return
@@ -409,6 +460,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, wl, world, rank)
+        elif args.workload == "cfg5":
+            run_decoder(args, wl, world, rank, local)
         else:
             run_ours(args, wl, world, rank, local)
     finally:
