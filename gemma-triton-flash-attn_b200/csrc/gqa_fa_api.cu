@@ -175,7 +175,7 @@ int launch(const CUtensorMap (&maps)[5], KParams p, cudaStream_t stream) {
 // Fixed configurations. Cfg<ROLE, M, D, DC, BN, NS, NSTAGES, YGROUP, BF16>
 template <bool BF16> using Fwd256 = Cfg<ROLE_FWD, 128, 256, 256, 128, 2, 8, 4, BF16>;
 template <bool BF16> using Dq256 = Cfg<ROLE_DQ, 128, 256, 256, 128, 1, 6, 2, BF16>;
-template <bool BF16> using Dk256 = Cfg<ROLE_DK, 128, 256, 256, 128, 1, 6, 2, BF16>;
+template <bool BF16> using Dk256 = PairCfg<ROLE_DK, 256, 128, 2, 8, BF16>;  // pair: faster than 1-CTA here
 template <bool BF16> using Dv256 = Cfg<ROLE_DV, 128, 256, 256, 128, 2, 8, 4, BF16>;
 template <bool BF16> using Fwd512 = Cfg<ROLE_FWD, 128, 512, 256, 128, 2, 6, 2, BF16>;
 // head_dim 512 backward: CTA pairs, PairCfg<ROLE, D, BN, NS, NSTAGES, BF16>
