@@ -66,6 +66,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU seconds per sample")
+    ap.add_argument("--strong", action="store_true",
+                    help="strong scaling: one config-2 problem (B=1) split over the GPUs by (batch, KV-group) units, "
+                         "and by sequence blocks when there are more GPUs than units; outputs all-gathered")
     ap.add_argument("--only", choices=["fwd", "dq", "dk", "dv"], default=None,
                     help="profiling mode: run only this kernel, warmup + steps launches, print nothing")
     return ap.parse_args()
@@ -422,6 +425,45 @@ def run_decoder(args, wl, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_strong(args, wl, world, rank, local):
+    """Strong scaling: the whole job is one problem; every rank ends with the
+    complete O, LSE, dQ, dK, dV (the all-gathers are inside the timed step)."""
+    from gemma_triton_flash_attn.flops import attn_flops
+    from gemma_triton_flash_attn.sharding import sharded_backward, sharded_forward, split_backward, split_forward
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(device)
+    B, Hq, Hkv, N, D, causal, W = (wl[x] for x in ("B", "Hq", "Hkv", "N", "D", "causal", "W"))
+    q, k, v, do = make_inputs(wl, 1234, device)  # same problem on every rank
+    split = world > B * Hkv
+    fwd, bwd = (split_forward, split_backward) if split else (sharded_forward, sharded_backward)
+
+    def step():
+        o, lse = fwd(q, k, v, causal, W)
+        bwd(q, k, v, o, lse, do, causal, W)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    with ClockSampler([uuid if uuid.startswith("GPU-") else "GPU-" + uuid]) as clocks:
+        ms = max_over_ranks(time_loop(step, args.steps, stream), world, device)
+    window = W if (causal and 0 < W < N) else 0
+    total = attn_flops(B, Hq, N, D, causal, window, bwd=True)
+    if rank == 0:
+        line = dict(metric=METRIC + " (strong scaling)", value=round(total / (ms * 1e-3) / 1e12, 2), unit="TFLOPS/s",
+                    n_gpus=world, steps=args.steps, warmup=args.warmup, ms_per_step=round(ms, 3),
+                    higher_is_better=True, scaling="strong", vs_baseline=None,
+                    dtype="bf16" if wl["dtype"] == torch.bfloat16 else "fp16", data="synthetic",
+                    config=dict(workload=wl["name"], global_batch=B, seq_len=N,
+                                parallelism=("sequence split of each (b, kv-group) unit" if split
+                                             else "(b, kv-group) units") + f" over {world} GPUs, outputs all-gathered"),
+                    clocks=clocks.summary(), gpu_launches=4 * args.steps)
+        print(json.dumps(line), flush=True)
+
+
 def run_reference(args, wl, world, rank):
     if rank != 0:
         return
@@ -462,6 +504,8 @@ def main():
             run_reference(args, wl, world, rank)
         elif args.workload == "cfg5":
             run_decoder(args, wl, world, rank, local)
+        elif args.strong:
+            run_strong(args, wl, world, rank, local)
         else:
             run_ours(args, wl, world, rank, local)
     finally:

@@ -47,7 +47,9 @@ struct KParams {
   int B, Hq, Hkv, N, G;
   int causal, window;  // window > 0 only meaningful with causal (reference semantics)
   float scale, scale_log2;
-  int num_row_tiles;
+  int num_row_tiles;  // row tiles in this launch
+  int tile_begin;     // first row tile (row-range launches; 0 otherwise)
+  int row_begin, row_end;  // host-side: rows this launch covers
   void* out;  // O / dQ / dK / dV, element strides below (last dim contiguous)
   long long out_sb, out_sh, out_sn;
   float* lse;    // [B, Hq, N] fp32, natural log, includes the softmax scale
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(256, 1)
   const int chunk = idx % C::NCHUNK;
   idx /= C::NCHUNK;
   // FWD/DQ: the last q tiles carry the most causal work, launch them first.
-  const int tile = C::ROWS_ARE_Q ? (p.num_row_tiles - 1 - idx) : idx;
+  const int tile = p.tile_begin + (C::ROWS_ARE_Q ? (p.num_row_tiles - 1 - idx) : idx);
   const int r0 = tile * M;
   const int N = p.N, G = p.G;
   const bool swa = p.causal && p.window > 0;

@@ -111,7 +111,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   idx /= heads;
   const int b = idx % p.B;
   idx /= p.B;
-  const int tile = C::ROWS_ARE_Q ? (p.num_row_tiles - 1 - idx) : idx;
+  const int tile = p.tile_begin + (C::ROWS_ARE_Q ? (p.num_row_tiles - 1 - idx) : idx);
   const int pr0 = tile * MP;
   const int r0 = pr0 + M * static_cast<int>(rank);
   const int N = p.N, G = p.G;

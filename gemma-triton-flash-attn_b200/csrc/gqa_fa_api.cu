@@ -156,7 +156,10 @@ int launch(const CUtensorMap (&maps)[5], KParams p, cudaStream_t stream) {
     if (e != cudaSuccess) return fail(GQAFA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_done_mask.fetch_or(bit);
   }
-  p.num_row_tiles = (p.N + C::MP - 1) / C::MP;
+  // Row range (whole sequence unless a *_rows entry point narrowed it); every
+  // kernel's row tile is 128 rows, and range starts are multiples of 128.
+  p.tile_begin = p.row_begin / C::MP;
+  p.num_row_tiles = (p.row_end + C::MP - 1) / C::MP - p.tile_begin;
   p.prof = g_prof_buffer.load(std::memory_order_relaxed);
   const long long heads = C::ROWS_ARE_Q ? p.Hq : p.Hkv;
   const long long grid = (long long)p.num_row_tiles * heads * p.B * C::NCHUNK * (C::PAIR ? 2 : 1);
@@ -185,6 +188,7 @@ template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 128, 2, 8, BF16>;
 
 struct Problem {
   int B, Hq, Hkv, N, D, causal, window;
+  int row_begin, row_end;  // rows of the row-tile dimension to compute
   float scale;
   bool bf16;
 };
@@ -212,6 +216,8 @@ int check_problem(int B, int Hq, int Hkv, int N, int D, float scale, int causal,
   pr->window = (pr->causal && window > 0 && window < N) ? window : 0;
   pr->scale = scale;
   pr->bf16 = (dtype == GQAFA_DTYPE_BF16);
+  pr->row_begin = 0;
+  pr->row_end = N;
   return GQAFA_OK;
 }
 
@@ -227,6 +233,8 @@ KParams base_params(const Problem& pr) {
   p.window = pr.window;
   p.scale = pr.scale;
   p.scale_log2 = pr.scale * 1.4426950408889634f;
+  p.row_begin = pr.row_begin;
+  p.row_end = pr.row_end;
   return p;
 }
 
@@ -321,15 +329,31 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
 
 using namespace gqafa;
 
-extern "C" int gqafa_fwd(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
-                         const void* v, const long long* v_strides, void* o, const long long* o_strides,
-                         float* lse, int batch, int heads_q, int heads_kv, int seqlen, int head_dim,
-                         float softmax_scale, int causal, int window, int dtype, void* stream) {
+// Rows of the row-tile dimension to compute: [row_begin, row_end), row_begin a
+// multiple of 128, row_end a multiple of 128 or N.
+static int set_rows(Problem* pr, int row_begin, int row_end) {
+  if (row_begin < 0 || row_end > pr->N || row_begin >= row_end || row_begin % 128 != 0 ||
+      (row_end % 128 != 0 && row_end != pr->N))
+    return fail(GQAFA_ERR_INVALID,
+                "row range [%d, %d) must satisfy 0 <= begin < end <= N=%d, begin a multiple of 128 and end a "
+                "multiple of 128 or N",
+                row_begin, row_end, pr->N);
+  pr->row_begin = row_begin;
+  pr->row_end = row_end;
+  return GQAFA_OK;
+}
+
+static int fwd_entry(int row_begin, int row_end, const void* q, const long long* q_strides, const void* k,
+                     const long long* k_strides, const void* v, const long long* v_strides, void* o,
+                     const long long* o_strides, float* lse, int batch, int heads_q, int heads_kv, int seqlen,
+                     int head_dim, float softmax_scale, int causal, int window, int dtype, void* stream) {
   g_last_error.clear();
-  Problem pr;
+  Problem pr{};
   int rc;
   if ((rc = check_problem(batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, window, dtype, &pr)))
     return rc;
+  if (row_end < 0) row_end = seqlen;
+  if ((rc = set_rows(&pr, row_begin, row_end))) return rc;
   TensorDesc qd, kd, vd, od;
   if ((rc = check_tensor("q", q, q_strides, batch, heads_q, seqlen, head_dim, &qd))) return rc;
   if ((rc = check_tensor("k", k, k_strides, batch, heads_kv, seqlen, head_dim, &kd))) return rc;
@@ -346,7 +370,24 @@ extern "C" int gqafa_fwd(const void* q, const long long* q_strides, const void* 
                  : fwd_impl<false, Fwd512<false>>(pr, qd, kd, vd, o, od, lse, st);
 }
 
-static int bwd_entry(int stages, const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+extern "C" int gqafa_fwd(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+                         const void* v, const long long* v_strides, void* o, const long long* o_strides,
+                         float* lse, int batch, int heads_q, int heads_kv, int seqlen, int head_dim,
+                         float softmax_scale, int causal, int window, int dtype, void* stream) {
+  return fwd_entry(0, -1, q, q_strides, k, k_strides, v, v_strides, o, o_strides, lse, batch, heads_q, heads_kv,
+                   seqlen, head_dim, softmax_scale, causal, window, dtype, stream);
+}
+
+extern "C" int gqafa_fwd_rows(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+                              const void* v, const long long* v_strides, void* o, const long long* o_strides,
+                              float* lse, int batch, int heads_q, int heads_kv, int seqlen, int head_dim,
+                              float softmax_scale, int causal, int window, int dtype, void* stream, int row_begin,
+                              int row_end) {
+  return fwd_entry(row_begin, row_end, q, q_strides, k, k_strides, v, v_strides, o, o_strides, lse, batch, heads_q,
+                   heads_kv, seqlen, head_dim, softmax_scale, causal, window, dtype, stream);
+}
+
+static int bwd_entry(int stages, int row_begin, int row_end, const void* q, const long long* q_strides, const void* k, const long long* k_strides,
                          const void* v, const long long* v_strides, const void* o, const long long* o_strides,
                          const void* dout, const long long* dout_strides, const float* lse, void* dq,
                          const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
@@ -355,10 +396,12 @@ static int bwd_entry(int stages, const void* q, const long long* q_strides, cons
                          void* stream) {
   g_last_error.clear();
   if (stages <= 0 || stages > 7) return fail(GQAFA_ERR_INVALID, "stage mask %d not in 1..7", stages);
-  Problem pr;
+  Problem pr{};
   int rc;
   if ((rc = check_problem(batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, window, dtype, &pr)))
     return rc;
+  if (row_end < 0) row_end = seqlen;
+  if ((rc = set_rows(&pr, row_begin, row_end))) return rc;
   TensorDesc qd, kd, vd, od, dod, dqd, dkd, dvd;
   if ((rc = check_tensor("q", q, q_strides, batch, heads_q, seqlen, head_dim, &qd))) return rc;
   if ((rc = check_tensor("k", k, k_strides, batch, heads_kv, seqlen, head_dim, &kd))) return rc;
@@ -395,14 +438,22 @@ static int bwd_entry(int stages, const void* q, const long long* q_strides, cons
       dk_strides, dv, dv_strides, delta, batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, \
       window, dtype, stream
 
-extern "C" int gqafa_bwd(GQAFA_BWD_PARAMS) { return bwd_entry(7, GQAFA_BWD_ARGS); }
+extern "C" int gqafa_bwd(GQAFA_BWD_PARAMS) { return bwd_entry(7, 0, -1, GQAFA_BWD_ARGS); }
 
 extern "C" int gqafa_bwd_stage(int stage, GQAFA_BWD_PARAMS) {
   if (stage < 0 || stage > 2) {
     g_last_error = "stage must be 0 (dQ + delta), 1 (dK) or 2 (dV)";
     return GQAFA_ERR_INVALID;
   }
-  return bwd_entry(1 << stage, GQAFA_BWD_ARGS);
+  return bwd_entry(1 << stage, 0, -1, GQAFA_BWD_ARGS);
+}
+
+extern "C" int gqafa_bwd_stage_rows(int stage, GQAFA_BWD_PARAMS, int row_begin, int row_end) {
+  if (stage < 0 || stage > 2) {
+    g_last_error = "stage must be 0 (dQ + delta), 1 (dK) or 2 (dV)";
+    return GQAFA_ERR_INVALID;
+  }
+  return bwd_entry(1 << stage, row_begin, row_end, GQAFA_BWD_ARGS);
 }
 
 // ---------------------------------------------------------------------------

@@ -28,6 +28,8 @@ EXPORTED_SYMBOLS = (
     "gqafa_bwd",
     "gqafa_bwd_stage",
     "gqafa_bwd_noalloc",
+    "gqafa_fwd_rows",
+    "gqafa_bwd_stage_rows",
     "gqafa_supported",
     "gqafa_last_error",
     "gqafa_device_status",
@@ -70,6 +72,10 @@ def load():
         lib.gqafa_bwd.restype = _I
         lib.gqafa_bwd_stage.argtypes = [_I] + lib.gqafa_bwd.argtypes
         lib.gqafa_bwd_stage.restype = _I
+        lib.gqafa_fwd_rows.argtypes = lib.gqafa_fwd.argtypes + [_I, _I]
+        lib.gqafa_fwd_rows.restype = _I
+        lib.gqafa_bwd_stage_rows.argtypes = [_I] + lib.gqafa_bwd.argtypes + [_I, _I]
+        lib.gqafa_bwd_stage_rows.restype = _I
         lib.gqafa_bwd_noalloc.argtypes = (
             [_P, _S, _P, _S, _P, _S, _P, _S, _P, _S, _P, _P, _S, _P, _S, _P, _S]
             + [_I, _I, _I, _I, _I, _F, _I, _I, _I, _P]

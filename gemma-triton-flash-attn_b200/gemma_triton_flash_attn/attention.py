@@ -169,17 +169,23 @@ class _DeviceScope:
         return False
 
 
-def _fwd(q, k, v, causal, window, scale, want_lse):
+def _fwd(q, k, v, causal, window, scale, want_lse, rows=None, out=None):
+    """Forward launch. `rows` = (begin, end) computes only those query rows,
+    into the preallocated `out` = (o, lse) (sequence-split multi-GPU path)."""
     lib = _lib.load()
     b, h_q, n, d = q.shape
     h_kv = k.shape[1]
     q, k, v = _abi_ready(q), _abi_ready(k), _abi_ready(v)
-    o = torch.empty_like(q)  # keeps q's layout (e.g. HF's (B, N, H, D) storage)
-    o = _abi_ready(o)
-    lse = torch.empty((b, h_q, n), dtype=torch.float32, device=q.device) if want_lse else None
+    if out is None:
+        o = torch.empty_like(q)  # keeps q's layout (e.g. HF's (B, N, H, D) storage)
+        o = _abi_ready(o)
+        lse = torch.empty((b, h_q, n), dtype=torch.float32, device=q.device) if want_lse else None
+    else:
+        o, lse = out
+    fn = lib.gqafa_fwd if rows is None else (lambda *a: lib.gqafa_fwd_rows(*a, int(rows[0]), int(rows[1])))
     with _DeviceScope(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        rc = lib.gqafa_fwd(
+        rc = fn(
             q.data_ptr(), _lib.strides_arg(q.stride()),
             k.data_ptr(), _lib.strides_arg(k.stride()),
             v.data_ptr(), _lib.strides_arg(v.stride()),
@@ -192,9 +198,11 @@ def _fwd(q, k, v, causal, window, scale, want_lse):
     return o, lse
 
 
-def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None):
+def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=None):
     """Backward launches. `stage` (0 dQ+delta, 1 dK, 2 dV) runs one kernel only,
-    into the buffers of `out` = (dq, dk, dv, delta) (profiling / benchmarks)."""
+    into the buffers of `out` = (dq, dk, dv, delta) (profiling / benchmarks);
+    with `rows` = (begin, end) only those rows (query rows for stage 0, key rows
+    for stages 1 and 2)."""
     lib = _lib.load()
     b, h_q, n, d = q.shape
     h_kv = k.shape[1]
@@ -207,7 +215,10 @@ def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None):
         delta = torch.empty((b, h_q, n), dtype=torch.float32, device=q.device)
     else:
         dq, dk, dv, delta = out
-    fn = lib.gqafa_bwd if stage is None else (lambda *a: lib.gqafa_bwd_stage(int(stage), *a))
+    if rows is not None:
+        fn = lambda *a: lib.gqafa_bwd_stage_rows(int(stage), *a, int(rows[0]), int(rows[1]))  # noqa: E731
+    else:
+        fn = lib.gqafa_bwd if stage is None else (lambda *a: lib.gqafa_bwd_stage(int(stage), *a))
     with _DeviceScope(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
         rc = fn(

@@ -17,12 +17,14 @@ stand-in; by default it is the CUDA kernel path.
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
 
-__all__ = ["ShardPlan", "sharded_forward", "sharded_backward"]
+__all__ = ["ShardPlan", "sharded_forward", "sharded_backward", "SequenceSplitPlan", "balanced_row_ranges",
+           "split_forward", "split_backward"]
 
 
 @dataclass(frozen=True)
@@ -147,3 +149,176 @@ def sharded_backward(q, k, v, o, lse, do, causal=False, slide_size=0, softmax_sc
         dk_loc = _gather_units(plan, dk_loc, group)
         dv_loc = _gather_units(plan, dv_loc, group)
     return (dq_loc.reshape(B, Hq, N, D), dk_loc.reshape(B, Hkv, N, D), dv_loc.reshape(B, Hkv, N, D))
+
+
+# --------------------------------------------------------------------------
+# Sequence split: more ranks than (batch, KV-group) units
+# --------------------------------------------------------------------------
+#
+# Config 2 at 8 GPUs has only B * H_KV = 4 units. Each unit is then split over
+# s = world / units ranks by blocks of 128 rows: a rank computes the O / LSE
+# and dQ rows of its query range, and the dK / dV rows of its key range. The
+# key-range stages read LSE and delta of every query row of the unit, so LSE
+# (after the forward) and delta (after the dQ stage) are all-gathered in
+# between; they are B * H_Q * N floats, small next to the outputs. Ranges are
+# chosen so that every rank of a unit gets about the same causal work.
+
+TILE = 128
+
+
+def tile_work(n: int, kind: str, causal: bool, window: int) -> list[int]:
+    """Attended pairs per 128-row tile: of its query rows (kind "q") or of its key rows (kind "k")."""
+    out = []
+    for t0 in range(0, n, TILE):
+        w = 0
+        for r in range(t0, min(n, t0 + TILE)):
+            if not causal:
+                w += n
+            elif kind == "q":
+                w += min(r + 1, window) if window else r + 1
+            else:
+                w += (min(n, r + window) if window else n) - r
+        out.append(w)
+    return out
+
+
+def balanced_row_ranges(n: int, parts: int, kind: str, causal: bool, window: int) -> list[tuple[int, int]]:
+    """Split [0, n) into `parts` contiguous ranges on 128-row boundaries with
+    about equal attention work; every range is non-empty when possible."""
+    work = tile_work(n, kind, causal, window)
+    tiles = len(work)
+    if parts > tiles:
+        raise ValueError(f"cannot split {tiles} row tiles into {parts} parts")
+    total = float(sum(work))
+    bounds, acc, t = [0], 0.0, 0
+    for part in range(1, parts):
+        target = total * part / parts
+        # advance while the next tile keeps us at or below the target, leaving
+        # at least one tile for each remaining part
+        while t < tiles - (parts - part) and acc + work[t] / 2 <= target:
+            acc += work[t]
+            t += 1
+        t = max(t, bounds[-1] + 1)
+        bounds.append(t)
+    bounds.append(tiles)
+    return [(b0 * TILE, min(n, b1 * TILE)) for b0, b1 in zip(bounds[:-1], bounds[1:])]
+
+
+@dataclass(frozen=True)
+class SequenceSplitPlan:
+    batch: int
+    heads_q: int
+    heads_kv: int
+    seqlen: int
+    world: int
+    causal: bool
+    window: int
+
+    @property
+    def units(self) -> int:
+        return self.batch * self.heads_kv
+
+    @property
+    def split(self) -> int:
+        if self.world % self.units != 0 or self.world < self.units:
+            raise ValueError(f"world {self.world} must be a multiple of the {self.units} (batch, KV-group) units")
+        return self.world // self.units
+
+    def assignment(self, rank: int):
+        """(b, kv_head, query rows, key rows) of `rank`."""
+        s = self.split
+        unit, part = divmod(rank, s)
+        b, kv = divmod(unit, self.heads_kv)
+        q_rows = balanced_row_ranges(self.seqlen, s, "q", self.causal, self.window)[part]
+        k_rows = balanced_row_ranges(self.seqlen, s, "k", self.causal, self.window)[part]
+        return b, kv, q_rows, k_rows
+
+
+def _gather_rows(plan, local: torch.Tensor, row_dim: int, which: str, group=None):
+    """All-gather each rank's row block (rows along `row_dim`) into a list
+    indexed by rank, each trimmed to that rank's row count."""
+    world = plan.world
+    idx = 2 if which == "q" else 3
+    counts = [plan.assignment(r)[idx][1] - plan.assignment(r)[idx][0] for r in range(world)]
+    m = max(counts)
+    shape = list(local.shape)
+    shape[row_dim] = m
+    pad = torch.zeros(shape, dtype=local.dtype, device=local.device)
+    pad.narrow(row_dim, 0, local.shape[row_dim]).copy_(local)
+    bufs = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(bufs, pad, group=group)
+    return [bufs[r].narrow(row_dim, 0, counts[r]) for r in range(world)]
+
+
+def split_forward(q, k, v, causal=False, slide_size=0, softmax_scale=None, group=None):
+    """Forward with each (batch, KV-group) unit split over several ranks by
+    query rows; returns the full (O, LSE) on every rank."""
+    from .attention import _check_inputs, _fwd, _normalize_window
+
+    _check_inputs(q, k, v)
+    B, Hq, N, D = q.shape
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    window = _normalize_window(causal, slide_size, N)
+    scale = (1.0 / math.sqrt(D)) if softmax_scale is None else float(softmax_scale)
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    plan = SequenceSplitPlan(B, Hq, Hkv, N, world, bool(causal), window)
+    b, kv, (q0, q1), _ = plan.assignment(rank)
+    hs = slice(kv * G, (kv + 1) * G)
+    qs, ks, vs = q[b:b + 1, hs], k[b:b + 1, kv:kv + 1], v[b:b + 1, kv:kv + 1]
+    o_loc = torch.empty_like(qs).contiguous()
+    lse_loc = torch.empty((1, G, N), dtype=torch.float32, device=q.device)
+    _fwd(qs, ks, vs, causal, window, scale, True, rows=(q0, q1), out=(o_loc, lse_loc))
+    o_parts = _gather_rows(plan, o_loc[:, :, q0:q1].contiguous(), 2, "q", group)
+    l_parts = _gather_rows(plan, lse_loc[:, :, q0:q1].contiguous(), 2, "q", group)
+    o = torch.empty_like(q)
+    lse = torch.empty((B, Hq, N), dtype=torch.float32, device=q.device)
+    for r in range(world):
+        rb, rkv, (r0, r1), _ = plan.assignment(r)
+        o[rb:rb + 1, rkv * G:(rkv + 1) * G, r0:r1] = o_parts[r]
+        lse[rb:rb + 1, rkv * G:(rkv + 1) * G, r0:r1] = l_parts[r]
+    return o, lse
+
+
+def split_backward(q, k, v, o, lse, do, causal=False, slide_size=0, softmax_scale=None, group=None):
+    """Backward of split_forward: dQ rows by query range, then (after
+    all-gathering delta) dK / dV rows by key range; full gradients on every rank."""
+    from .attention import _bwd, _check_inputs, _normalize_window
+
+    _check_inputs(q, k, v)
+    B, Hq, N, D = q.shape
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    window = _normalize_window(causal, slide_size, N)
+    scale = (1.0 / math.sqrt(D)) if softmax_scale is None else float(softmax_scale)
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    plan = SequenceSplitPlan(B, Hq, Hkv, N, world, bool(causal), window)
+    b, kv, (q0, q1), (k0, k1) = plan.assignment(rank)
+    hs = slice(kv * G, (kv + 1) * G)
+    args = (q[b:b + 1, hs], k[b:b + 1, kv:kv + 1], v[b:b + 1, kv:kv + 1], o[b:b + 1, hs],
+            lse[b:b + 1, hs].contiguous(), do[b:b + 1, hs])
+    dq_loc = torch.empty((1, G, N, D), dtype=q.dtype, device=q.device)
+    dk_loc = torch.empty((1, 1, N, D), dtype=k.dtype, device=q.device)
+    dv_loc = torch.empty((1, 1, N, D), dtype=v.dtype, device=q.device)
+    delta = torch.empty((1, G, N), dtype=torch.float32, device=q.device)
+    bufs = (dq_loc, dk_loc, dv_loc, delta)
+    _bwd(*args, causal, window, scale, stage=0, out=bufs, rows=(q0, q1))
+    d_parts = _gather_rows(plan, delta[:, :, q0:q1].contiguous(), 2, "q", group)
+    for r in range(world):
+        rb, rkv, (r0, r1), _ = plan.assignment(r)
+        if (rb, rkv) == (b, kv):
+            delta[:, :, r0:r1] = d_parts[r]
+    _bwd(*args, causal, window, scale, stage=1, out=bufs, rows=(k0, k1))
+    _bwd(*args, causal, window, scale, stage=2, out=bufs, rows=(k0, k1))
+    dq_parts = _gather_rows(plan, dq_loc[:, :, q0:q1].contiguous(), 2, "q", group)
+    dk_parts = _gather_rows(plan, dk_loc[:, :, k0:k1].contiguous(), 2, "k", group)
+    dv_parts = _gather_rows(plan, dv_loc[:, :, k0:k1].contiguous(), 2, "k", group)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    for r in range(world):
+        rb, rkv, (r0, r1), (s0, s1) = plan.assignment(r)
+        dq[rb:rb + 1, rkv * G:(rkv + 1) * G, r0:r1] = dq_parts[r]
+        dk[rb:rb + 1, rkv:rkv + 1, s0:s1] = dk_parts[r]
+        dv[rb:rb + 1, rkv:rkv + 1, s0:s1] = dv_parts[r]
+    return dq, dk, dv

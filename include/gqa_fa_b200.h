@@ -104,6 +104,28 @@ GQAFA_API int gqafa_bwd_noalloc(const void* q, const long long* q_strides, const
                                 int head_dim, float softmax_scale, int causal, int window, int dtype,
                                 void* stream);
 
+/* Row-range variants for splitting one (batch, KV-group) unit across GPUs
+ * by sequence blocks (no counterpart in the reference, whose launches always
+ * cover every row). Same arguments as gqafa_fwd / gqafa_bwd_stage plus
+ * [row_begin, row_end): row_begin a multiple of 128, row_end a multiple of 128
+ * or N. gqafa_fwd_rows writes the O and LSE rows of that query range (keys:
+ * all). gqafa_bwd_stage_rows stage 0 writes the dQ and delta rows of that
+ * query range; stages 1 and 2 write the dK / dV rows of that key range and
+ * read lse and delta of every query row, so those must be complete. */
+GQAFA_API int gqafa_fwd_rows(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+                             const void* v, const long long* v_strides, void* o, const long long* o_strides,
+                             float* lse, int batch, int heads_q, int heads_kv, int seqlen, int head_dim,
+                             float softmax_scale, int causal, int window, int dtype, void* stream, int row_begin,
+                             int row_end);
+GQAFA_API int gqafa_bwd_stage_rows(int stage, const void* q, const long long* q_strides, const void* k,
+                                   const long long* k_strides, const void* v, const long long* v_strides,
+                                   const void* o, const long long* o_strides, const void* dout,
+                                   const long long* dout_strides, const float* lse, void* dq,
+                                   const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
+                                   const long long* dv_strides, float* delta, int batch, int heads_q,
+                                   int heads_kv, int seqlen, int head_dim, float softmax_scale, int causal,
+                                   int window, int dtype, void* stream, int row_begin, int row_end);
+
 /* 1 if (head_dim, dtype) has a compiled kernel set, else 0. */
 GQAFA_API int gqafa_supported(int head_dim, int dtype);
 

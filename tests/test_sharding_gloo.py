@@ -107,3 +107,30 @@ def test_rank_failure_surfaces_as_error_not_hang(tmp_path):
         assert not p.is_alive()
     assert os.path.exists(os.path.join(tmp_path, "error"))
     assert not os.path.exists(os.path.join(tmp_path, "completed"))
+
+
+@pytest.mark.parametrize("n,parts,causal,window", [(16384, 2, True, 0), (16384, 4, True, 1024), (1000, 3, True, 0),
+                                                   (200, 2, True, 0), (4096, 2, False, 0)])
+@pytest.mark.parametrize("kind", ["q", "k"])
+def test_sequence_split_ranges_cover_and_balance(n, parts, causal, window, kind):
+    from gemma_triton_flash_attn.sharding import balanced_row_ranges, tile_work
+
+    r = balanced_row_ranges(n, parts, kind, causal, window)
+    assert r[0][0] == 0 and r[-1][1] == n and len(r) == parts
+    for (a0, a1), (b0, b1) in zip(r[:-1], r[1:]):
+        assert a1 == b0 and a0 % 128 == 0 and a0 < a1
+    w = tile_work(n, kind, causal, window)
+    per = [sum(w[a // 128:(b + 127) // 128]) for a, b in r]
+    if n >= 4096:
+        assert max(per) <= 1.1 * min(per), per
+
+
+def test_sequence_split_plan_assignment():
+    from gemma_triton_flash_attn.sharding import SequenceSplitPlan
+
+    plan = SequenceSplitPlan(1, 32, 4, 16384, 8, True, 0)
+    a = [plan.assignment(r) for r in range(8)]
+    assert [(x[0], x[1]) for x in a] == [(0, kv) for kv in range(4) for _ in range(2)]
+    assert a[0][2] == a[2][2] and a[0][2] != a[1][2]
+    with pytest.raises(ValueError):
+        SequenceSplitPlan(1, 32, 4, 16384, 6, True, 0).split

@@ -19,38 +19,42 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _inputs(device):
+def _inputs(device, split=False):
     g = torch.Generator().manual_seed(11)
-    B, Hq, Hkv, N, D = 2, 16, 2, 640, 512
+    B, Hq, Hkv, N, D = (1, 8, 1, 1000, 512) if split else (2, 16, 2, 640, 512)
     mk = lambda *s: (torch.randn(*s, generator=g) * 0.5).bfloat16().to(device)  # noqa: E731
     return mk(B, Hq, N, D), mk(B, Hkv, N, D), mk(B, Hkv, N, D), mk(B, Hq, N, D)
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, split=False):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
     try:
-        from gemma_triton_flash_attn.sharding import sharded_backward, sharded_forward
+        from gemma_triton_flash_attn.sharding import sharded_backward, sharded_forward, split_backward, split_forward
 
-        q, k, v, do = _inputs(f"cuda:{rank}")
-        o, lse = sharded_forward(q, k, v, True, 0)
-        dq, dk, dv = sharded_backward(q, k, v, o, lse, do, True, 0)
+        q, k, v, do = _inputs(f"cuda:{rank}", split)
+        fwd, bwd = (split_forward, split_backward) if split else (sharded_forward, sharded_backward)
+        o, lse = fwd(q, k, v, True, 0)
+        dq, dk, dv = bwd(q, k, v, o, lse, do, True, 0)
         torch.save({n: t.cpu() for n, t in dict(o=o, lse=lse, dq=dq, dk=dk, dv=dv).items()},
                    os.path.join(out_dir, f"r{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
-def test_sharded_equals_single_gpu(tmp_path):
+@pytest.mark.parametrize("split", [False, True], ids=["units", "sequence_split"])
+def test_sharded_equals_single_gpu(tmp_path, split):
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs at least two GPUs")
+    if split:
+        world = 2  # one (batch, KV-group) unit split over two ranks by sequence blocks
     from gemma_triton_flash_attn.attention import flash_attn_gqa_backward, flash_attn_gqa_forward_with_lse
 
-    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
-    q, k, v, do = _inputs("cuda:0")
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), split), nprocs=world, join=True)
+    q, k, v, do = _inputs("cuda:0", split)
     o, lse = flash_attn_gqa_forward_with_lse(q, k, v, True, 0)
     dq, dk, dv = flash_attn_gqa_backward(q, k, v, o, lse, do, True, 0)
     ref = dict(o=o, lse=lse, dq=dq, dk=dk, dv=dv)
