@@ -429,7 +429,8 @@ def run_strong(args, wl, world, rank, local):
     """Strong scaling: the whole job is one problem; every rank ends with the
     complete O, LSE, dQ, dK, dV (the all-gathers are inside the timed step)."""
     from gemma_triton_flash_attn.flops import attn_flops
-    from gemma_triton_flash_attn.sharding import sharded_backward, sharded_forward, split_backward, split_forward
+    from gemma_triton_flash_attn.sharding import (head_split_backward, head_split_forward, sharded_backward,
+                                                  sharded_forward)
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -437,7 +438,7 @@ def run_strong(args, wl, world, rank, local):
     B, Hq, Hkv, N, D, causal, W = (wl[x] for x in ("B", "Hq", "Hkv", "N", "D", "causal", "W"))
     q, k, v, do = make_inputs(wl, 1234, device)  # same problem on every rank
     split = world > B * Hkv
-    fwd, bwd = (split_forward, split_backward) if split else (sharded_forward, sharded_backward)
+    fwd, bwd = (head_split_forward, head_split_backward) if split else (sharded_forward, sharded_backward)
 
     def step():
         o, lse = fwd(q, k, v, causal, W)
@@ -458,8 +459,9 @@ def run_strong(args, wl, world, rank, local):
                     higher_is_better=True, scaling="strong", vs_baseline=None,
                     dtype="bf16" if wl["dtype"] == torch.bfloat16 else "fp16", data="synthetic",
                     config=dict(workload=wl["name"], global_batch=B, seq_len=N,
-                                parallelism=("sequence split of each (b, kv-group) unit" if split
-                                             else "(b, kv-group) units") + f" over {world} GPUs, outputs all-gathered"),
+                                parallelism=("query heads of each (b, kv-group) unit split, dK/dV all-reduced"
+                                             if split else "(b, kv-group) units")
+                                + f" over {world} GPUs, outputs all-gathered"),
                     clocks=clocks.summary(), gpu_launches=4 * args.steps)
         print(json.dumps(line), flush=True)
 

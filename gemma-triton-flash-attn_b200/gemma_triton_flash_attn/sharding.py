@@ -17,6 +17,7 @@ stand-in; by default it is the CUDA kernel path.
 """
 from __future__ import annotations
 
+import functools
 import math
 from dataclasses import dataclass
 
@@ -24,7 +25,8 @@ import torch
 import torch.distributed as dist
 
 __all__ = ["ShardPlan", "sharded_forward", "sharded_backward", "SequenceSplitPlan", "balanced_row_ranges",
-           "split_forward", "split_backward"]
+           "split_forward", "split_backward", "head_split_assignment", "head_split_forward",
+           "head_split_backward"]
 
 
 @dataclass(frozen=True)
@@ -182,6 +184,7 @@ def tile_work(n: int, kind: str, causal: bool, window: int) -> list[int]:
     return out
 
 
+@functools.lru_cache(maxsize=256)
 def balanced_row_ranges(n: int, parts: int, kind: str, causal: bool, window: int) -> list[tuple[int, int]]:
     """Split [0, n) into `parts` contiguous ranges on 128-row boundaries with
     about equal attention work; every range is non-empty when possible."""
@@ -224,6 +227,7 @@ class SequenceSplitPlan:
             raise ValueError(f"world {self.world} must be a multiple of the {self.units} (batch, KV-group) units")
         return self.world // self.units
 
+    @functools.lru_cache(maxsize=1024)  # noqa: B019 - plans are small, frozen and few
     def assignment(self, rank: int):
         """(b, kv_head, query rows, key rows) of `rank`."""
         s = self.split
@@ -322,3 +326,78 @@ def split_backward(q, k, v, o, lse, do, causal=False, slide_size=0, softmax_scal
         dk[rb:rb + 1, rkv:rkv + 1, s0:s1] = dk_parts[r]
         dv[rb:rb + 1, rkv:rkv + 1, s0:s1] = dv_parts[r]
     return dq, dk, dv
+
+
+# --------------------------------------------------------------------------
+# Head split: more ranks than units, each unit's query heads divided
+# --------------------------------------------------------------------------
+#
+# The preferred way to use more ranks than (batch, KV-group) units: the s
+# ranks of a unit each take G/s of its query heads over the whole sequence.
+# Forward and dQ need nothing from the other ranks; dK and dV of the unit's KV
+# head are the sum of the s ranks' partial results (each over its G/s heads),
+# the path's one real reduction, done with an all-reduce in fp32. Every kernel
+# keeps its full-sequence grid, unlike the sequence split, whose dK/dV launches
+# shrink to one KV head and a fraction of its rows.
+
+
+def head_split_assignment(batch: int, heads_q: int, heads_kv: int, world: int, rank: int):
+    """(b, kv_head, first query head, number of query heads) of `rank`."""
+    units = batch * heads_kv
+    if world % units != 0 or world < units:
+        raise ValueError(f"world {world} must be a multiple of the {units} (batch, KV-group) units")
+    s = world // units
+    g = heads_q // heads_kv
+    if g % s != 0:
+        raise ValueError(f"{s} ranks per unit do not divide its {g} query heads")
+    unit, part = divmod(rank, s)
+    b, kv = divmod(unit, heads_kv)
+    return b, kv, kv * g + part * (g // s), g // s
+
+
+def head_split_forward(q, k, v, causal=False, slide_size=0, softmax_scale=None, group=None):
+    """Forward with each unit's query heads divided over s ranks; full (O, LSE) on every rank."""
+    from .attention import flash_attn_gqa_forward_with_lse
+
+    B, Hq, N, D = q.shape
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    b, kv, h0, nh = head_split_assignment(B, Hq, k.shape[1], world, rank)
+    o_loc, l_loc = flash_attn_gqa_forward_with_lse(q[b:b + 1, h0:h0 + nh], k[b:b + 1, kv:kv + 1],
+                                                   v[b:b + 1, kv:kv + 1], causal, slide_size, softmax_scale)
+    o_parts = [torch.empty_like(o_loc) for _ in range(world)]
+    l_parts = [torch.empty_like(l_loc) for _ in range(world)]
+    dist.all_gather(o_parts, o_loc.contiguous(), group=group)
+    dist.all_gather(l_parts, l_loc.contiguous(), group=group)
+    o = torch.empty_like(q)
+    lse = torch.empty((B, Hq, N), dtype=torch.float32, device=q.device)
+    for r in range(world):
+        rb, _, rh0, rnh = head_split_assignment(B, Hq, k.shape[1], world, r)
+        o[rb:rb + 1, rh0:rh0 + rnh] = o_parts[r]
+        lse[rb:rb + 1, rh0:rh0 + rnh] = l_parts[r]
+    return o, lse
+
+
+def head_split_backward(q, k, v, o, lse, do, causal=False, slide_size=0, softmax_scale=None, group=None):
+    """Backward of head_split_forward: dQ per rank, dK/dV summed over the ranks
+    of each unit (fp32 all-reduce); full gradients on every rank."""
+    from .attention import flash_attn_gqa_backward
+
+    B, Hq, N, D = q.shape
+    Hkv = k.shape[1]
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    b, kv, h0, nh = head_split_assignment(B, Hq, Hkv, world, rank)
+    hs = slice(h0, h0 + nh)
+    dq_loc, dk_loc, dv_loc = flash_attn_gqa_backward(
+        q[b:b + 1, hs], k[b:b + 1, kv:kv + 1], v[b:b + 1, kv:kv + 1], o[b:b + 1, hs],
+        lse[b:b + 1, hs].contiguous(), do[b:b + 1, hs], causal, slide_size, softmax_scale)
+    dq_parts = [torch.empty_like(dq_loc) for _ in range(world)]
+    dist.all_gather(dq_parts, dq_loc.contiguous(), group=group)
+    dq = torch.empty_like(q)
+    for r in range(world):
+        rb, _, rh0, rnh = head_split_assignment(B, Hq, Hkv, world, r)
+        dq[rb:rb + 1, rh0:rh0 + rnh] = dq_parts[r]
+    dkv = torch.zeros((2, B, Hkv, N, D), dtype=torch.float32, device=q.device)
+    dkv[0, b, kv] = dk_loc[0, 0].float()
+    dkv[1, b, kv] = dv_loc[0, 0].float()
+    dist.all_reduce(dkv, group=group)
+    return dq, dkv[0].to(k.dtype), dkv[1].to(v.dtype)

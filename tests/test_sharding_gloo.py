@@ -134,3 +134,12 @@ def test_sequence_split_plan_assignment():
     assert a[0][2] == a[2][2] and a[0][2] != a[1][2]
     with pytest.raises(ValueError):
         SequenceSplitPlan(1, 32, 4, 16384, 6, True, 0).split
+
+
+def test_head_split_assignment():
+    from gemma_triton_flash_attn.sharding import head_split_assignment
+
+    got = [head_split_assignment(1, 32, 4, 8, r) for r in range(8)]
+    assert got == [(0, kv, kv * 8 + p * 4, 4) for kv in range(4) for p in range(2)]
+    with pytest.raises(ValueError):
+        head_split_assignment(1, 12, 4, 8, 0)  # 3 heads per group, 2 ranks per unit
