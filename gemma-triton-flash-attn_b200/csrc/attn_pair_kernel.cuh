@@ -39,12 +39,16 @@ struct PairCfg {
   static constexpr int PANELS_D = D / 64;
   static constexpr int R_PANEL = M * 128;
   static constexpr int R_BYTES = PANELS_D * R_PANEL * (HAS_DP ? 2 : 1);
-  static constexpr int STAGE_BYTES = BN * 128;          // one Y panel (BN rows) or two C panels
-  static constexpr int C_PANEL_BYTES = (BN / 2) * 128;  // BN/2 rows of one 64-column panel
-  static constexpr int C_STAGES = PANELS_D / 2;
-  static constexpr int C_BOX = BN / 2, Y_BOX = BN;
+  // Ring stages are 16 KB: 128 rows of one 64-column panel.
+  static constexpr int STAGE_BYTES = 128 * 128;
+  static constexpr int CR = BN / 2;                     // score-operand rows this CTA loads per item
+  static constexpr int CP = 128 / CR;                   // score-operand panels per stage (2 or 1)
+  static constexpr int C_PANEL_BYTES = CR * 128;
+  static constexpr int C_STAGES = PANELS_D / CP;
+  static constexpr int C_BOX = CR, Y_BOX = 128;
   static constexpr int NACC = D / 256;                  // N=256 accumulate instructions per k-step
-  static constexpr int Y_STAGES = NACC * 2;             // this CTA's 128 of every 256 columns
+  static constexpr int YH = BN / 128;                   // 128-row stages per accumulate panel
+  static constexpr int Y_STAGES = NACC * 2 * YH;        // this CTA's 128 of every 256 columns
   static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;
   static constexpr int PBUF_ONE = M * BN * 2;
   static constexpr int PBUF_BYTES = NS * PBUF_ONE;
@@ -57,7 +61,7 @@ struct PairCfg {
   static constexpr uint32_t IDESC_Y = make_idesc(MP, 256, BF16, true);
 
   static_assert(D % 256 == 0, "D");
-  static_assert(BN == 128, "BN");
+  static_assert(BN == 128 || BN == 256, "BN");
   static_assert(ACC_COLS + NS * SBUF_COLS * (HAS_DP ? 2 : 1) <= 512, "TMEM");
   static_assert(NSTAGES % 2 == 0, "ring groups");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
@@ -198,9 +202,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           int st;
           if (!acquire(st)) return false;
           const uint32_t full_l = mapa_shared(BAR_FULL(st), 0);
-          for (int pp = 0; pp < 2; ++pp)
+          for (int pp = 0; pp < C::CP; ++pp)
             tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES + pp * C::C_PANEL_BYTES), m, full_l,
-                             64 * (2 * s + pp), c0 + static_cast<int>(rank) * (BN / 2), hc, b);
+                             64 * (C::CP * s + pp), c0 + static_cast<int>(rank) * C::CR, hc, b);
         }
         return true;
       };
@@ -214,13 +218,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       };
       auto load_y = [&](int i) -> bool {
         const int c0 = item_col0(i), hc = item_headC(i);
+        // stage order: [instruction g][128-row half hh][panel j]; the two panels of
+        // one (g, hh) are adjacent, which is the MN-major operand's LBO.
         for (int g = 0; g < C::NACC; ++g)
-          for (int j = 0; j < 2; ++j) {
-            int st;
-            if (!acquire(st)) return false;
-            tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES), &tmY, mapa_shared(BAR_FULL(st), 0),
-                             64 * (4 * g + 2 * static_cast<int>(rank) + j), c0, hc, b);
-          }
+          for (int hh = 0; hh < C::YH; ++hh)
+            for (int j = 0; j < 2; ++j) {
+              int st;
+              if (!acquire(st)) return false;
+              tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES), &tmY, mapa_shared(BAR_FULL(st), 0),
+                               64 * (4 * g + 2 * static_cast<int>(rank) + j), c0 + 128 * hh, hc, b);
+            }
         return true;
       };
       for (int s = 0; s < NS && s < n_items && ok; ++s) ok = load_scores(s);
@@ -255,10 +262,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           tc_fence_after();
           const uint64_t bst = dRingK + static_cast<uint64_t>((st * C::STAGE_BYTES) >> 4);
 #pragma unroll
-          for (int pp = 0; pp < 2; ++pp) {
+          for (int pp = 0; pp < C::CP; ++pp) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              const uint64_t ad = dR + static_cast<uint64_t>(((2 * s + pp) * C::R_PANEL + 32 * k) >> 4);
+              const uint64_t ad = dR + static_cast<uint64_t>(((C::CP * s + pp) * C::R_PANEL + 32 * k) >> 4);
               const uint64_t bd = bst + static_cast<uint64_t>((pp * C::C_PANEL_BYTES + 32 * k) >> 4);
               mma_ss_pair(d_tmem, ad, bd, C::IDESC_S, (s | pp | k) != 0);
             }
@@ -283,30 +290,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         if (!mbar_wait_cluster(BAR_PREADY(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY))
           return false;
         tock(WC_MMA_PREADY, t0);
-        t0 = tick();
-        for (int j = 0; j < C::Y_STAGES; ++j) {
-          const int st = (cnt + j) % NST;
-          if (!mbar_wait_cluster(BAR_FULL(st), ((cnt + j) / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL))
-            return false;
-        }
-        tock(WC_MMA_FULL_Y, t0);
-        tc_fence_after();
+        // Accumulate operand stages are consumed two at a time (the two panels of
+        // one instruction g and 128-row half hh) and released right after their
+        // MMAs, so an item never needs more ring stages at once than the ring has.
         const uint64_t pb = dP + static_cast<uint64_t>((sb * C::PBUF_ONE) >> 4);
-        uint64_t yb[C::NACC];
-#pragma unroll
-        for (int g = 0; g < C::NACC; ++g)
-          yb[g] = dRingMN + static_cast<uint64_t>((((cnt + 2 * g) % NST) * C::STAGE_BYTES) >> 4);
         const uint32_t acc0 = (i > 0) ? 1u : 0u;
 #pragma unroll
-        for (int t = 0; t < BN / 16; ++t) {
-          const uint64_t ad = pb + static_cast<uint64_t>(((t / 4) * (M * 128) + (t % 4) * 32) >> 4);
+        for (int g = 0; g < C::NACC; ++g) {
 #pragma unroll
-          for (int g = 0; g < C::NACC; ++g)
-            mma_ss_pair(tbase + g * 128, ad, yb[g] + static_cast<uint64_t>((t * 2048) >> 4), C::IDESC_Y,
-                        t > 0 ? 1u : acc0);
+          for (int hh = 0; hh < C::YH; ++hh) {
+            const uint32_t c2 = cnt + 2 * (g * C::YH + hh);
+            t0 = tick();
+            for (int j = 0; j < 2; ++j) {
+              if (!mbar_wait_cluster(BAR_FULL((c2 + j) % NST), ((c2 + j) / NST) & 1u, abort_flag, p.status,
+                                     ST_TIMEOUT_RING_FULL))
+                return false;
+            }
+            tock(WC_MMA_FULL_Y, t0);
+            tc_fence_after();
+            const uint64_t yb = dRingMN + static_cast<uint64_t>(((c2 % NST) * C::STAGE_BYTES) >> 4);
+#pragma unroll
+            for (int tt = 0; tt < 8 && hh * 8 + tt < BN / 16; ++tt) {
+              const int t = hh * 8 + tt;
+              const uint64_t ad = pb + static_cast<uint64_t>(((t / 4) * (M * 128) + (t % 4) * 32) >> 4);
+              mma_ss_pair(tbase + g * 128, ad, yb + static_cast<uint64_t>((tt * 2048) >> 4), C::IDESC_Y,
+                          t > 0 ? 1u : acc0);
+            }
+            mma_commit_pair(BAR_EMPTY(c2 % NST));
+            mma_commit_pair(BAR_EMPTY((c2 + 1) % NST));
+          }
         }
         mma_commit_pair(BAR_ACC);
-        for (int j = 0; j < C::Y_STAGES; ++j) mma_commit_pair(BAR_EMPTY((cnt + j) % NST));
         cnt += C::Y_STAGES;
         return true;
       };
@@ -394,49 +408,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       const unsigned span = span_of(lo_rel, hi_abs - cb);
       const uint32_t s_col = C::ACC_COLS + sb * C::SBUF_COLS;
       const uint32_t dp_col = C::ACC_COLS + (NS + sb) * C::SBUF_COLS;
-      uint32_t rs[KCH][32], rd[KCH][32];
+      constexpr int KB = KCH < 2 ? KCH : 2;  // chunks loaded per TMEM round trip (register budget)
 #pragma unroll
-      for (int k = 0; k < KCH; ++k) {
-        tmem_ld32_async(tq + s_col + 32 * k, rs[k]);
-        if constexpr (C::HAS_DP) tmem_ld32_async(tq + dp_col + 32 * k, rd[k]);
-      }
+      for (int kb = 0; kb < KCH; kb += KB) {
+        uint32_t rs[KB][32], rd[KB][32];
 #pragma unroll
-      for (int k = 0; k < KCH; ++k) {
-        tmem_ld_wait32(rs[k]);
-        if constexpr (C::HAS_DP) tmem_ld_wait32(rd[k]);
-      }
-#pragma unroll
-      for (int k = 0; k < KCH; ++k) {
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float l2, dl;
-          if constexpr (C::ROWS_ARE_Q) {
-            l2 = row_lse2;
-            dl = row_delta;
-          } else {
-            l2 = __shfl_sync(0xffffffffu, col_lse2[k], j);
-            dl = C::HAS_DP ? __shfl_sync(0xffffffffu, col_delta[k], j) : 0.f;
-          }
-          float pv = ex2(__uint_as_float(rs[k][j]) * sl2 - l2);
-          pv = (static_cast<unsigned>(32 * k + j - lo_rel) < span) ? pv : 0.f;
-          if constexpr (C::HAS_DP) {
-            v[j] = pv * (__uint_as_float(rd[k][j]) - dl);
-          } else {
-            v[j] = pv;
-          }
+        for (int u = 0; u < KB; ++u) {
+          tmem_ld32_async(tq + s_col + 32 * (kb + u), rs[u]);
+          if constexpr (C::HAS_DP) tmem_ld32_async(tq + dp_col + 32 * (kb + u), rd[u]);
         }
-        // K-major SWIZZLE_128B [64 rows x BN] tile: this thread's half is panel `half`.
-        uint8_t* prow = sP + sb * C::PBUF_ONE + half * (M * 128) + row * 128;
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int chunk16 = 4 * k + cc;
-          uint4 w;
-          w.x = pack2<C::BF16>(v[8 * cc + 0], v[8 * cc + 1]);
-          w.y = pack2<C::BF16>(v[8 * cc + 2], v[8 * cc + 3]);
-          w.z = pack2<C::BF16>(v[8 * cc + 4], v[8 * cc + 5]);
-          w.w = pack2<C::BF16>(v[8 * cc + 6], v[8 * cc + 7]);
-          *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (row & 7)) * 16)) = w;
+        for (int u = 0; u < KB; ++u) {
+          tmem_ld_wait32(rs[u]);
+          if constexpr (C::HAS_DP) tmem_ld_wait32(rd[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < KB; ++u) {
+          const int k = kb + u;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float l2, dl;
+            if constexpr (C::ROWS_ARE_Q) {
+              l2 = row_lse2;
+              dl = row_delta;
+            } else {
+              l2 = __shfl_sync(0xffffffffu, col_lse2[k], j);
+              dl = C::HAS_DP ? __shfl_sync(0xffffffffu, col_delta[k], j) : 0.f;
+            }
+            float pv = ex2(__uint_as_float(rs[u][j]) * sl2 - l2);
+            pv = (static_cast<unsigned>(32 * k + j - lo_rel) < span) ? pv : 0.f;
+            if constexpr (C::HAS_DP) {
+              v[j] = pv * (__uint_as_float(rd[u][j]) - dl);
+            } else {
+              v[j] = pv;
+            }
+          }
+          // K-major SWIZZLE_128B [64 rows x BN] tile of 64-column panels.
+          const int col = half * (BN / 2) + 32 * k;  // column within the item
+          uint8_t* prow = sP + sb * C::PBUF_ONE + (col / 64) * (M * 128) + row * 128;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int chunk16 = (col % 64) / 8 + cc;
+            uint4 w;
+            w.x = pack2<C::BF16>(v[8 * cc + 0], v[8 * cc + 1]);
+            w.y = pack2<C::BF16>(v[8 * cc + 2], v[8 * cc + 3]);
+            w.z = pack2<C::BF16>(v[8 * cc + 4], v[8 * cc + 5]);
+            w.w = pack2<C::BF16>(v[8 * cc + 6], v[8 * cc + 7]);
+            *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (row & 7)) * 16)) = w;
+          }
         }
       }
       tc_fence_before();

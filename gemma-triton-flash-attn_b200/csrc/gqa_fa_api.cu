@@ -181,10 +181,12 @@ template <bool BF16> using Dq256 = Cfg<ROLE_DQ, 128, 256, 256, 128, 1, 6, 2, BF1
 template <bool BF16> using Dk256 = PairCfg<ROLE_DK, 256, 128, 2, 8, BF16>;  // pair: faster than 1-CTA here
 template <bool BF16> using Dv256 = Cfg<ROLE_DV, 128, 256, 256, 128, 2, 8, 4, BF16>;
 template <bool BF16> using Fwd512 = Cfg<ROLE_FWD, 128, 512, 256, 128, 2, 6, 2, BF16>;
-// head_dim 512 backward: CTA pairs, PairCfg<ROLE, D, BN, NS, NSTAGES, BF16>
-template <bool BF16> using Dq512 = PairCfg<ROLE_DQ, 512, 128, 2, 4, BF16>;
-template <bool BF16> using Dk512 = PairCfg<ROLE_DK, 512, 128, 2, 4, BF16>;
-template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 128, 2, 8, BF16>;
+// head_dim 512 backward: CTA pairs, PairCfg<ROLE, D, BN, NS, NSTAGES, BF16>. 256-column items make
+// every score MMA an N=256 pair instruction (full tensor rate; N=128 pair MMAs run at 70%), at the
+// price of single-buffered S/dP in TMEM for dQ and dK (256 + 128 + 128 columns).
+template <bool BF16> using Dq512 = PairCfg<ROLE_DQ, 512, 256, 1, 4, BF16>;
+template <bool BF16> using Dk512 = PairCfg<ROLE_DK, 512, 256, 1, 4, BF16>;
+template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 256, 2, 6, BF16>;
 
 struct Problem {
   int B, Hq, Hkv, N, D, causal, window;
