@@ -52,7 +52,7 @@ struct PairCfg {
   static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;
   static constexpr int PBUF_ONE = M * BN * 2;
   static constexpr int PBUF_BYTES = NS * PBUF_ONE;
-  static constexpr int NBARS = 2 * NSTAGES + 1 + 2 * NS + 2;
+  static constexpr int NBARS = 2 * NSTAGES + 1 + 3 * NS + 2;
   static constexpr int MISC_BYTES = M * 4 + NBARS * 8 + 16;
   static constexpr int SMEM_BYTES = 1024 + R_BYTES + RING_BYTES + PBUF_BYTES + MISC_BYTES;
   static constexpr int ACC_COLS = D / 2;
@@ -96,6 +96,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   // rather than on BAR_ACC: with two score buffers BAR_ACC can still be two
   // phases short of the end, where its parity is indistinguishable.
   const uint32_t BAR_FINAL = bar0 + 8u * (2 * NST + 2 + 2 * NS);
+  // S of the item is in TMEM (dP may still be in flight): lets the row warps
+  // compute P while the dP MMAs run (dQ / dK).
+  auto BAR_SREADY = [&](int s) { return bar0 + 8u * (2 * NST + 3 + 2 * NS + s); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -146,6 +149,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     mbar_init(BAR_RFULL, 1);
     for (int s = 0; s < NS; ++s) {
       mbar_init(BAR_SFULL(s), 1);
+      mbar_init(BAR_SREADY(s), 1);
       mbar_init(BAR_PREADY(s), 8);  // 4 row warps in each CTA of the pair
     }
     mbar_init(BAR_ACC, 1);
@@ -279,6 +283,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const int sb = i % NS;
         if (!scores_from(dR1, tbase + C::ACC_COLS + sb * C::SBUF_COLS)) return false;
         if constexpr (C::HAS_DP) {
+          mma_commit_pair(BAR_SREADY(sb));
           if (!scores_from(dR2, tbase + C::ACC_COLS + (NS + sb) * C::SBUF_COLS)) return false;
         }
         mma_commit_pair(BAR_SFULL(sb));
@@ -396,7 +401,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         }
       }
       const long long t_w = tick();
-      ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
+      // dQ / dK: wait for S only; dP is waited for after P is computed.
+      ok = mbar_wait_cluster(C::HAS_DP ? BAR_SREADY(sb) : BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status,
+                             ST_TIMEOUT_SCORES);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tock(WC_ROW_SFULL, t_w);
@@ -409,18 +416,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       const uint32_t s_col = C::ACC_COLS + sb * C::SBUF_COLS;
       const uint32_t dp_col = C::ACC_COLS + (NS + sb) * C::SBUF_COLS;
       constexpr int KB = KCH < 2 ? KCH : 2;  // chunks loaded per TMEM round trip (register budget)
+      // P = exp2(S * scale * log2 e - lse * log2 e), masked, for all columns this thread owns.
+      float pv[KCH][32];
 #pragma unroll
       for (int kb = 0; kb < KCH; kb += KB) {
-        uint32_t rs[KB][32], rd[KB][32];
+        uint32_t rs[KB][32];
+#pragma unroll
+        for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + s_col + 32 * (kb + u), rs[u]);
+#pragma unroll
+        for (int u = 0; u < KB; ++u) tmem_ld_wait32(rs[u]);
 #pragma unroll
         for (int u = 0; u < KB; ++u) {
-          tmem_ld32_async(tq + s_col + 32 * (kb + u), rs[u]);
-          if constexpr (C::HAS_DP) tmem_ld32_async(tq + dp_col + 32 * (kb + u), rd[u]);
+          const int k = kb + u;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float l2 = C::ROWS_ARE_Q ? row_lse2 : __shfl_sync(0xffffffffu, col_lse2[k], j);
+            const float e = ex2(__uint_as_float(rs[u][j]) * sl2 - l2);
+            pv[k][j] = (static_cast<unsigned>(32 * k + j - lo_rel) < span) ? e : 0.f;
+          }
         }
+      }
+      if constexpr (C::HAS_DP) {
+        ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+      }
 #pragma unroll
-        for (int u = 0; u < KB; ++u) {
-          tmem_ld_wait32(rs[u]);
-          if constexpr (C::HAS_DP) tmem_ld_wait32(rd[u]);
+      for (int kb = 0; kb < KCH; kb += KB) {
+        uint32_t rd[KB][32];
+        if constexpr (C::HAS_DP) {
+#pragma unroll
+          for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + dp_col + 32 * (kb + u), rd[u]);
+#pragma unroll
+          for (int u = 0; u < KB; ++u) tmem_ld_wait32(rd[u]);
         }
 #pragma unroll
         for (int u = 0; u < KB; ++u) {
@@ -428,20 +457,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            float l2, dl;
-            if constexpr (C::ROWS_ARE_Q) {
-              l2 = row_lse2;
-              dl = row_delta;
-            } else {
-              l2 = __shfl_sync(0xffffffffu, col_lse2[k], j);
-              dl = C::HAS_DP ? __shfl_sync(0xffffffffu, col_delta[k], j) : 0.f;
-            }
-            float pv = ex2(__uint_as_float(rs[u][j]) * sl2 - l2);
-            pv = (static_cast<unsigned>(32 * k + j - lo_rel) < span) ? pv : 0.f;
             if constexpr (C::HAS_DP) {
-              v[j] = pv * (__uint_as_float(rd[u][j]) - dl);
+              const float dl = C::ROWS_ARE_Q ? row_delta : __shfl_sync(0xffffffffu, col_delta[k], j);
+              v[j] = pv[k][j] * (__uint_as_float(rd[u][j]) - dl);
             } else {
-              v[j] = pv;
+              v[j] = pv[k][j];
             }
           }
           // K-major SWIZZLE_128B [64 rows x BN] tile of 64-column panels.
