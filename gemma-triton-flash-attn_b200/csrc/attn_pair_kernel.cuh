@@ -1,8 +1,8 @@
-// Head_dim-512 backward kernels on CTA pairs (cta_group::2).
+// Head_dim-512 kernels on CTA pairs (cta_group::2).
 //
-// Same roles and math as attn_kernel.cuh (ROLE_DQ / ROLE_DK / ROLE_DV; the
-// reference launches they replace are listed there), but a row tile of 128
-// rows is shared by the two CTAs of a cluster, 64 rows each:
+// Same roles and math as attn_kernel.cuh (ROLE_FWD / ROLE_DQ / ROLE_DK /
+// ROLE_DV; the reference launches they replace are listed there), but a row
+// tile of 128 rows is shared by the two CTAs of a cluster, 64 rows each:
 //
 //   * every tcgen05.mma is issued by the even CTA (the leader) with
 //     cta_group::2 and M = 128: A comes from each CTA's own 64 rows, B is split
@@ -13,7 +13,8 @@
 //   * the fp32 accumulator of 64 rows x 512 columns takes 256 TMEM columns per
 //     CTA (the 2x2 layout: lanes 0-63 hold the first half of each N range,
 //     lanes 64-127 the second half), which leaves room for double-buffered
-//     score buffers.
+//     score buffers. For the forward this is what removes the 1-CTA kernel's
+//     second pass: the whole 512-column O fits, so S is computed once.
 //
 // Synchronisation across the pair: TMA loads of both CTAs complete on the
 // leader's "full" barriers (the leader expects both CTAs' bytes); the
@@ -35,7 +36,7 @@ struct PairCfg {
   static constexpr int MP = 128;   // rows per pair
   static constexpr int NCHUNK = 1;
   static constexpr bool HAS_DP = (ROLE == ROLE_DQ || ROLE == ROLE_DK);
-  static constexpr bool ROWS_ARE_Q = (ROLE == ROLE_DQ);
+  static constexpr bool ROWS_ARE_Q = (ROLE == ROLE_DQ || ROLE == ROLE_FWD);
   static constexpr int PANELS_D = D / 64;
   static constexpr int R_PANEL = M * 128;
   static constexpr int R_BYTES = PANELS_D * R_PANEL * (HAS_DP ? 2 : 1);
@@ -53,7 +54,10 @@ struct PairCfg {
   static constexpr int PBUF_ONE = M * BN * 2;
   static constexpr int PBUF_BYTES = NS * PBUF_ONE;
   static constexpr int NBARS = 2 * NSTAGES + 1 + 3 * NS + 2;
-  static constexpr int MISC_BYTES = M * 4 + NBARS * 8 + 16;
+  // sRow (M floats), then for the forward the row-statistics exchange:
+  // [2 slots][2 halves][M] maxima and [2 halves][M] partial sums.
+  static constexpr int XCH_FLOATS = (ROLE == ROLE_FWD) ? 6 * M : 0;
+  static constexpr int MISC_BYTES = M * 4 + XCH_FLOATS * 4 + NBARS * 8 + 16;
   static constexpr int SMEM_BYTES = 1024 + R_BYTES + RING_BYTES + PBUF_BYTES + MISC_BYTES;
   static constexpr int ACC_COLS = D / 2;
   static constexpr int SBUF_COLS = BN / 2;
@@ -65,7 +69,6 @@ struct PairCfg {
   static_assert(ACC_COLS + NS * SBUF_COLS * (HAS_DP ? 2 : 1) <= 512, "TMEM");
   static_assert(NSTAGES % 2 == 0, "ring groups");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
-  static_assert(ROLE != ROLE_FWD, "backward roles only");
 };
 
 template <class C>
@@ -81,7 +84,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   uint8_t* sRing = smem + C::R_BYTES;
   uint8_t* sP = sRing + C::RING_BYTES;
   float* sRow = reinterpret_cast<float*>(sP + C::PBUF_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + M);
+  float* sX = sRow + M;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sX + C::XCH_FLOATS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -383,135 +387,293 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     }
 
     constexpr int KCH = C::SBUF_COLS / 32;  // 32-column chunks this thread owns per item
-    for (int i = 0; i < n_items && ok; ++i) {
-      const int sb = i % NS;
-      const int c0 = item_col0(i);
-      const int cb = c0 + half * (BN / 2);  // first column this thread owns
-      // Per-column softmax statistics (DK / DV), fetched before waiting so the
-      // global-load latency overlaps the MMAs.
-      float col_lse2[KCH], col_delta[KCH];
-      if constexpr (!C::ROWS_ARE_Q) {
-        const int hq = item_headC(i);
-        const long long colbase = (static_cast<long long>(b) * p.Hq + hq) * N;
-#pragma unroll
-        for (int k = 0; k < KCH; ++k) {
-          const int qq = cb + 32 * k + lane;
-          col_lse2[k] = (qq < N) ? p.lse[colbase + qq] * LOG2E : 0.f;
-          col_delta[k] = (C::HAS_DP && qq < N) ? p.delta[colbase + qq] : 0.f;
+    if constexpr (C::ROLE == ROLE_FWD) {
+      // Online softmax (exp2 domain, lazy rescaling as in attn_kernel.cuh) over
+      // the BN/2 columns of every item this thread holds. The two warps holding
+      // the same 64 rows (quadrants q and q^2) exchange their maxima through
+      // shared memory once per item, so both halves of a row share one running
+      // max; each keeps a partial row sum, added in the epilogue. The exchange
+      // barrier runs on every item even after a failed wait, so a partner warp
+      // is never left at it.
+      const int pbar = 2 + (q4 & 1);
+      auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(pbar) : "memory"); };
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int i = 0; i < n_items; ++i) {
+        const int sb = i % NS;
+        const int cb = item_col0(i) + half * (BN / 2);
+        const long long t_w = tick();
+        if (ok) {
+          ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
+          ok = __all_sync(0xffffffffu, ok);
         }
-      }
-      const long long t_w = tick();
-      // dQ / dK: wait for S only; dP is waited for after P is computed.
-      ok = mbar_wait_cluster(C::HAS_DP ? BAR_SREADY(sb) : BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status,
-                             ST_TIMEOUT_SCORES);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tock(WC_ROW_SFULL, t_w);
-      const long long t_work = tick();
-      tc_fence_after();
-      int lo_abs, hi_abs;
-      attended_interval(C::ROWS_ARE_Q, r0 + row, N, p.causal, p.window, lo_abs, hi_abs);
-      const int lo_rel = lo_abs - cb;
-      const unsigned span = span_of(lo_rel, hi_abs - cb);
-      const uint32_t s_col = C::ACC_COLS + sb * C::SBUF_COLS;
-      const uint32_t dp_col = C::ACC_COLS + (NS + sb) * C::SBUF_COLS;
-      constexpr int KB = KCH < 2 ? KCH : 2;  // chunks loaded per TMEM round trip (register budget)
-      // P = exp2(S * scale * log2 e - lse * log2 e), masked, for all columns this thread owns.
-      float pv[KCH][32];
+        tock(WC_ROW_SFULL, t_w);
+        const long long t_work = tick();
+        const uint32_t s_col = C::ACC_COLS + sb * C::SBUF_COLS;
+        float s[KCH][32];
+        float mx = -INFINITY;
+        if (ok) {
+          tc_fence_after();
+          int lo_abs, hi_abs;
+          attended_interval(true, r0 + row, N, p.causal, p.window, lo_abs, hi_abs);
+          const int lo_rel = lo_abs - cb;
+          const unsigned span = span_of(lo_rel, hi_abs - cb);
+          constexpr int KB = KCH < 2 ? KCH : 2;
 #pragma unroll
-      for (int kb = 0; kb < KCH; kb += KB) {
-        uint32_t rs[KB][32];
+          for (int kb = 0; kb < KCH; kb += KB) {
+            uint32_t rs[KB][32];
 #pragma unroll
-        for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + s_col + 32 * (kb + u), rs[u]);
+            for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + s_col + 32 * (kb + u), rs[u]);
 #pragma unroll
-        for (int u = 0; u < KB; ++u) tmem_ld_wait32(rs[u]);
+            for (int u = 0; u < KB; ++u) tmem_ld_wait32(rs[u]);
 #pragma unroll
-        for (int u = 0; u < KB; ++u) {
-          const int k = kb + u;
+            for (int u = 0; u < KB; ++u) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float l2 = C::ROWS_ARE_Q ? row_lse2 : __shfl_sync(0xffffffffu, col_lse2[k], j);
-            const float e = ex2(__uint_as_float(rs[u][j]) * sl2 - l2);
-            pv[k][j] = (static_cast<unsigned>(32 * k + j - lo_rel) < span) ? e : 0.f;
-          }
-        }
-      }
-      if constexpr (C::HAS_DP) {
-        ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
-      }
-#pragma unroll
-      for (int kb = 0; kb < KCH; kb += KB) {
-        uint32_t rd[KB][32];
-        if constexpr (C::HAS_DP) {
-#pragma unroll
-          for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + dp_col + 32 * (kb + u), rd[u]);
-#pragma unroll
-          for (int u = 0; u < KB; ++u) tmem_ld_wait32(rd[u]);
-        }
-#pragma unroll
-        for (int u = 0; u < KB; ++u) {
-          const int k = kb + u;
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if constexpr (C::HAS_DP) {
-              const float dl = C::ROWS_ARE_Q ? row_delta : __shfl_sync(0xffffffffu, col_delta[k], j);
-              v[j] = pv[k][j] * (__uint_as_float(rd[u][j]) - dl);
-            } else {
-              v[j] = pv[k][j];
+              for (int j = 0; j < 32; ++j) {
+                const int c = 32 * (kb + u) + j;
+                const float x = __uint_as_float(rs[u][j]) * sl2;
+                s[kb + u][j] = (static_cast<unsigned>(c - lo_rel) < span) ? x : -INFINITY;
+                mx = fmaxf(mx, s[kb + u][j]);
+              }
             }
           }
+        }
+        float* xm = sX + (i & 1) * 2 * M;
+        xm[half * M + row] = mx;
+        pair_sync();
+        mx = fmaxf(mx, xm[(half ^ 1) * M + row]);
+        if (!ok) continue;
+        float alpha = 1.f;
+        bool rescale = false;
+        const float m_new = fmaxf(m_run, mx);
+        if (m_new > m_run + 8.f) {
+          if (i > 0) {
+            alpha = ex2(m_run - m_new);
+            rescale = true;
+          }
+          m_run = m_new;
+        }
+        const float ms = (m_run == -INFINITY) ? 0.f : m_run;
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < KCH; ++k) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            s[k][j] = ex2(s[k][j] - ms);
+            sum += s[k][j];
+          }
+        }
+        l_run = l_run * alpha + sum;
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O's rows are rescaled in place once the previous item's P V
+          // MMAs have landed (this thread's quadrant, all ACC_COLS columns).
+          ok = mbar_wait_cluster(BAR_ACC, (i - 1) & 1u, abort_flag, p.status, ST_TIMEOUT_ACC);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) continue;
+          tc_fence_after();
+#pragma unroll 1
+          for (int k = 0; k < C::ACC_COLS / 32; k += 2) {
+            uint32_t r[2][32];
+            tmem_ld32_async(tq + 32 * k, r[0]);
+            tmem_ld32_async(tq + 32 * (k + 1), r[1]);
+            tmem_ld_wait32(r[0]);
+            tmem_ld_wait32(r[1]);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) r[u][j] = __float_as_uint(__uint_as_float(r[u][j]) * alpha);
+              tmem_st32(tq + 32 * (k + u), r[u]);
+            }
+          }
+          tmem_st_wait();
+        }
+#pragma unroll
+        for (int k = 0; k < KCH; ++k) {
           // K-major SWIZZLE_128B [64 rows x BN] tile of 64-column panels.
-          const int col = half * (BN / 2) + 32 * k;  // column within the item
+          const int col = half * (BN / 2) + 32 * k;
           uint8_t* prow = sP + sb * C::PBUF_ONE + (col / 64) * (M * 128) + row * 128;
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
             const int chunk16 = (col % 64) / 8 + cc;
             uint4 w;
-            w.x = pack2<C::BF16>(v[8 * cc + 0], v[8 * cc + 1]);
-            w.y = pack2<C::BF16>(v[8 * cc + 2], v[8 * cc + 3]);
-            w.z = pack2<C::BF16>(v[8 * cc + 4], v[8 * cc + 5]);
-            w.w = pack2<C::BF16>(v[8 * cc + 6], v[8 * cc + 7]);
+            w.x = pack2<C::BF16>(s[k][8 * cc + 0], s[k][8 * cc + 1]);
+            w.y = pack2<C::BF16>(s[k][8 * cc + 2], s[k][8 * cc + 3]);
+            w.z = pack2<C::BF16>(s[k][8 * cc + 4], s[k][8 * cc + 5]);
+            w.w = pack2<C::BF16>(s[k][8 * cc + 6], s[k][8 * cc + 7]);
             *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (row & 7)) * 16)) = w;
           }
         }
+        tc_fence_before();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(pready_l0 + 8u * sb);
+        tock(WC_ROW_WORK, t_work);
       }
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote(pready_l0 + 8u * sb);
-      tock(WC_ROW_WORK, t_work);
-    }
 
-    // ---------------- epilogue ----------------
-    const long long t_epi = tick();
-    if (ok && n_items > 0) {
-      ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
-      ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok && n_items > 0) {
-      tc_fence_after();
-      const float mul = (C::ROLE == ROLE_DV) ? 1.f : p.scale;
-      const int orow = r0 + row;
-      const long long obase = static_cast<long long>(b) * p.out_sb + static_cast<long long>(h) * p.out_sh +
-                              static_cast<long long>(orow) * p.out_sn;
+      // ---------------- epilogue ----------------
+      const long long t_epi = tick();
+      float* xl = sX + 4 * M;
+      xl[half * M + row] = l_run;
+      pair_sync();
+      const float l_tot = l_run + xl[(half ^ 1) * M + row];
+      if (ok && n_items > 0) {
+        ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok && n_items > 0) {
+        tc_fence_after();
+        const float mul = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
+        const int orow = r0 + row;
+        const long long obase = static_cast<long long>(b) * p.out_sb + static_cast<long long>(h) * p.out_sh +
+                                static_cast<long long>(orow) * p.out_sn;
 #pragma unroll 1
-      for (int g = 0; g < C::NACC; ++g) {
+        for (int g = 0; g < C::NACC; ++g) {
 #pragma unroll 1
-        for (int k = 0; k < 4; ++k) {
-          uint32_t r[32];
-          tmem_ld32(tq + g * 128 + 32 * k, r);
-          float v[32];
+          for (int k = 0; k < 4; ++k) {
+            uint32_t r[32];
+            tmem_ld32(tq + g * 128 + 32 * k, r);
+            float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * mul;
-          if (orow < N) store_row32<C::BF16>(p.out, obase + 256 * g + 128 * half + 32 * k, v);
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * mul;
+            if (orow < N) store_row32<C::BF16>(p.out, obase + 256 * g + 128 * half + 32 * k, v);
+          }
+        }
+        if (p.lse != nullptr && half == 0 && orow < N) {
+          const float LN2 = 0.6931471805599453f;
+          p.lse[rowbase_q + orow] = (l_tot > 0.f) ? (m_run + __log2f(l_tot)) * LN2 : -INFINITY;
         }
       }
+      tock(WC_ROW_EPILOGUE, t_epi);
+    } else {
+      for (int i = 0; i < n_items && ok; ++i) {
+        const int sb = i % NS;
+        const int c0 = item_col0(i);
+        const int cb = c0 + half * (BN / 2);  // first column this thread owns
+        // Per-column softmax statistics (DK / DV), fetched before waiting so the
+        // global-load latency overlaps the MMAs.
+        float col_lse2[KCH], col_delta[KCH];
+        if constexpr (!C::ROWS_ARE_Q) {
+          const int hq = item_headC(i);
+          const long long colbase = (static_cast<long long>(b) * p.Hq + hq) * N;
+#pragma unroll
+          for (int k = 0; k < KCH; ++k) {
+            const int qq = cb + 32 * k + lane;
+            col_lse2[k] = (qq < N) ? p.lse[colbase + qq] * LOG2E : 0.f;
+            col_delta[k] = (C::HAS_DP && qq < N) ? p.delta[colbase + qq] : 0.f;
+          }
+        }
+        const long long t_w = tick();
+        // dQ / dK: wait for S only; dP is waited for after P is computed.
+        ok = mbar_wait_cluster(C::HAS_DP ? BAR_SREADY(sb) : BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status,
+                               ST_TIMEOUT_SCORES);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tock(WC_ROW_SFULL, t_w);
+        const long long t_work = tick();
+        tc_fence_after();
+        int lo_abs, hi_abs;
+        attended_interval(C::ROWS_ARE_Q, r0 + row, N, p.causal, p.window, lo_abs, hi_abs);
+        const int lo_rel = lo_abs - cb;
+        const unsigned span = span_of(lo_rel, hi_abs - cb);
+        const uint32_t s_col = C::ACC_COLS + sb * C::SBUF_COLS;
+        const uint32_t dp_col = C::ACC_COLS + (NS + sb) * C::SBUF_COLS;
+        constexpr int KB = KCH < 2 ? KCH : 2;  // chunks loaded per TMEM round trip (register budget)
+        // P = exp2(S * scale * log2 e - lse * log2 e), masked, for all columns this thread owns.
+        float pv[KCH][32];
+#pragma unroll
+        for (int kb = 0; kb < KCH; kb += KB) {
+          uint32_t rs[KB][32];
+#pragma unroll
+          for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + s_col + 32 * (kb + u), rs[u]);
+#pragma unroll
+          for (int u = 0; u < KB; ++u) tmem_ld_wait32(rs[u]);
+#pragma unroll
+          for (int u = 0; u < KB; ++u) {
+            const int k = kb + u;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float l2 = C::ROWS_ARE_Q ? row_lse2 : __shfl_sync(0xffffffffu, col_lse2[k], j);
+              const float e = ex2(__uint_as_float(rs[u][j]) * sl2 - l2);
+              pv[k][j] = (static_cast<unsigned>(32 * k + j - lo_rel) < span) ? e : 0.f;
+            }
+          }
+        }
+        if constexpr (C::HAS_DP) {
+          ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int kb = 0; kb < KCH; kb += KB) {
+          uint32_t rd[KB][32];
+          if constexpr (C::HAS_DP) {
+#pragma unroll
+            for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + dp_col + 32 * (kb + u), rd[u]);
+#pragma unroll
+            for (int u = 0; u < KB; ++u) tmem_ld_wait32(rd[u]);
+          }
+#pragma unroll
+          for (int u = 0; u < KB; ++u) {
+            const int k = kb + u;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if constexpr (C::HAS_DP) {
+                const float dl = C::ROWS_ARE_Q ? row_delta : __shfl_sync(0xffffffffu, col_delta[k], j);
+                v[j] = pv[k][j] * (__uint_as_float(rd[u][j]) - dl);
+              } else {
+                v[j] = pv[k][j];
+              }
+            }
+            // K-major SWIZZLE_128B [64 rows x BN] tile of 64-column panels.
+            const int col = half * (BN / 2) + 32 * k;  // column within the item
+            uint8_t* prow = sP + sb * C::PBUF_ONE + (col / 64) * (M * 128) + row * 128;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              const int chunk16 = (col % 64) / 8 + cc;
+              uint4 w;
+              w.x = pack2<C::BF16>(v[8 * cc + 0], v[8 * cc + 1]);
+              w.y = pack2<C::BF16>(v[8 * cc + 2], v[8 * cc + 3]);
+              w.z = pack2<C::BF16>(v[8 * cc + 4], v[8 * cc + 5]);
+              w.w = pack2<C::BF16>(v[8 * cc + 6], v[8 * cc + 7]);
+              *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (row & 7)) * 16)) = w;
+            }
+          }
+        }
+        tc_fence_before();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(pready_l0 + 8u * sb);
+        tock(WC_ROW_WORK, t_work);
+      }
+
+      // ---------------- epilogue ----------------
+      const long long t_epi = tick();
+      if (ok && n_items > 0) {
+        ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok && n_items > 0) {
+        tc_fence_after();
+        const float mul = (C::ROLE == ROLE_DV) ? 1.f : p.scale;
+        const int orow = r0 + row;
+        const long long obase = static_cast<long long>(b) * p.out_sb + static_cast<long long>(h) * p.out_sh +
+                                static_cast<long long>(orow) * p.out_sn;
+#pragma unroll 1
+        for (int g = 0; g < C::NACC; ++g) {
+#pragma unroll 1
+          for (int k = 0; k < 4; ++k) {
+            uint32_t r[32];
+            tmem_ld32(tq + g * 128 + 32 * k, r);
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * mul;
+            if (orow < N) store_row32<C::BF16>(p.out, obase + 256 * g + 128 * half + 32 * k, v);
+          }
+        }
+      }
+      tock(WC_ROW_EPILOGUE, t_epi);
     }
-    tock(WC_ROW_EPILOGUE, t_epi);
   }
 
   if (prof) {

@@ -5,8 +5,7 @@
 //   head_dim 256  forward  M=128 BN=128, one 256-column O chunk
 //                 dQ, dK   M=128 BN=128, single-buffered scores (TMEM: 256+128+128)
 //                 dV       M=128 BN=128, double-buffered scores
-//   head_dim 512  forward  M=128 BN=128, two 256-column O chunks (grid dimension)
-//                 dQ/dK/dV M=64  BN=64, accumulator in the lower TMEM half-quadrants
+//   head_dim 512  all      CTA pairs (attn_pair_kernel.cuh), 64 rows per CTA, BN=256
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -180,10 +179,11 @@ template <bool BF16> using Fwd256 = Cfg<ROLE_FWD, 128, 256, 256, 128, 2, 8, 4, B
 template <bool BF16> using Dq256 = Cfg<ROLE_DQ, 128, 256, 256, 128, 1, 6, 2, BF16>;
 template <bool BF16> using Dk256 = PairCfg<ROLE_DK, 256, 128, 2, 8, BF16>;  // pair: faster than 1-CTA here
 template <bool BF16> using Dv256 = Cfg<ROLE_DV, 128, 256, 256, 128, 2, 8, 4, BF16>;
-template <bool BF16> using Fwd512 = Cfg<ROLE_FWD, 128, 512, 256, 128, 2, 6, 2, BF16>;
-// head_dim 512 backward: CTA pairs, PairCfg<ROLE, D, BN, NS, NSTAGES, BF16>. 256-column items make
+// head_dim 512: CTA pairs, PairCfg<ROLE, D, BN, NS, NSTAGES, BF16>. The forward keeps all 512 O
+// columns in TMEM (256 per CTA), so S is computed once per item. 256-column items make
 // every score MMA an N=256 pair instruction (full tensor rate; N=128 pair MMAs run at 70%), at the
 // price of single-buffered S/dP in TMEM for dQ and dK (256 + 128 + 128 columns).
+template <bool BF16> using Fwd512 = PairCfg<ROLE_FWD, 512, 256, 2, 6, BF16>;
 template <bool BF16> using Dq512 = PairCfg<ROLE_DQ, 512, 256, 1, 4, BF16>;
 template <bool BF16> using Dk512 = PairCfg<ROLE_DK, 512, 256, 1, 4, BF16>;
 template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 256, 2, 6, BF16>;
@@ -253,8 +253,13 @@ int fwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
   CUtensorMap maps[5];
   int rc;
   if ((rc = encode_map(&maps[0], q, pr.B, pr.N, pr.D, CF::M, BF16))) return rc;
-  if ((rc = encode_map(&maps[2], k, pr.B, pr.N, pr.D, CF::BN, BF16))) return rc;
-  if ((rc = encode_map(&maps[4], v, pr.B, pr.N, pr.D, CF::BN, BF16))) return rc;
+  int cbox = CF::BN, ybox = CF::BN;
+  if constexpr (CF::PAIR) {
+    cbox = CF::C_BOX;
+    ybox = CF::Y_BOX;
+  }
+  if ((rc = encode_map(&maps[2], k, pr.B, pr.N, pr.D, cbox, BF16))) return rc;
+  if ((rc = encode_map(&maps[4], v, pr.B, pr.N, pr.D, ybox, BF16))) return rc;
   maps[1] = maps[0];
   maps[3] = maps[2];
   KParams p = base_params(pr);
