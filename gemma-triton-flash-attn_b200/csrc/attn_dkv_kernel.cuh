@@ -1,0 +1,271 @@
+// Head_dim-512 dK + dV from materialised P and dS (CTA pairs, cta_group::2).
+//
+// Replaces the reference's packed dK/dV launch (flash_attn/attention.py:
+// 1602-1620) when the dQ kernel has written P and dS to a workspace (see
+// KParams::ws). The reference's kernel recomputes S = Q K^T and dP = dO V^T
+// for every (key tile, query block); here they were computed once, by the dQ
+// kernel, so this kernel is two accumulations per (query tile, key tile):
+//
+//   dV[k rows] += P^T dO      dK[k rows] += dS^T Q      (dK scaled at the end)
+//
+// A pair owns 128 key rows (64 per CTA). Both fp32 accumulators stay in TMEM
+// for the whole kernel: dK in columns 0-255, dV in 256-511 of each CTA, in
+// the 2x2 layout of attn_pair_kernel.cuh. P^T and dS^T are read as MN-major A
+// operands straight from the workspace's [128 queries][256 keys] blocks (a TMA
+// box of 64 keys x 128 queries per CTA); Q and dO are MN-major B operands
+// split along head_dim between the two CTAs, as in the other pair kernels.
+//
+// Per query tile ("sub-item") the ring carries 10 stages of 16 KB in this
+// order: dS^T, P^T, then for g = 0, 1 the two 64-column panels of Q and the
+// two of dO for head_dim columns 256g + 128 * rank + [0, 128). The A stages
+// are held for the whole sub-item, the B stages are released in pairs, so
+// the ring needs at least 10 stages. Every wait is bounded as elsewhere.
+#pragma once
+#include "attn_kernel.cuh"
+
+namespace gqafa {
+
+template <int D_, int NSTAGES_, bool BF16_>
+struct DkvCfg {
+  static constexpr int D = D_, NSTAGES = NSTAGES_;
+  static constexpr bool BF16 = BF16_;
+  static constexpr bool PAIR = true;
+  static constexpr bool ROWS_ARE_Q = false;
+  static constexpr int NCHUNK = 1;
+  static constexpr int M = 64, MP = 128;
+  static constexpr int BN = 256;            // query rows per item (two 128-row query tiles)
+  static constexpr int NACC = D / 256;      // N=256 pair instructions per accumulator and k-step
+  static constexpr int STAGE_BYTES = 128 * 128;
+  static constexpr int SUB_STAGES = 2 + 4 * NACC;
+  static constexpr int Y_BOX = 128;
+  static constexpr int NBARS = 2 * NSTAGES + 1;
+  static constexpr int SMEM_BYTES = 1024 + NSTAGES * STAGE_BYTES + NBARS * 8 + 16;
+  static constexpr uint32_t IDESC = make_idesc(MP, 256, BF16, true, true);
+
+  static_assert(D == 512, "the dK/dV accumulators fill TMEM exactly at head_dim 512");
+  static_assert(NSTAGES % 2 == 0 && NSTAGES >= SUB_STAGES, "ring");
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
+
+template <class C>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+    attn_dkv_kernel(const __grid_constant__ CUtensorMap tmWS, const __grid_constant__ CUtensorMap tmQ,
+                    const __grid_constant__ CUtensorMap tmDO, const KParams p) {
+  constexpr int M = C::M, MP = C::MP, NST = C::NSTAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sRing = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + NST * C::STAGE_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR_FULL = [&](int s) { return bar0 + 8u * s; };
+  auto BAR_EMPTY = [&](int s) { return bar0 + 8u * (NST + s); };
+  const uint32_t BAR_FINAL = bar0 + 8u * (2 * NST);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = (rank == 0);
+
+  // ---- tile decode: one pair per (key tile, KV head, batch), heaviest first
+  int idx = blockIdx.x >> 1;
+  const int h = idx % p.Hkv;
+  idx /= p.Hkv;
+  const int b = idx % p.B;
+  idx /= p.B;
+  const int tile = p.tile_begin + idx;
+  const int pr0 = tile * MP;
+  const int r0 = pr0 + M * static_cast<int>(rank);
+  const int N = p.N, G = p.G;
+  const int T = (N + 127) / 128;
+  const bool swa = p.causal && p.window > 0;
+  // Query tiles whose rows can attend this pair's keys.
+  const int t_lo = p.causal ? pr0 / 128 : 0;
+  const int t_hi = swa ? min(T, (pr0 + MP - 1 + p.window - 1) / 128 + 1) : T;
+  const int kblk = pr0 / 256;                        // key block of the workspace
+  const int kcol = (pr0 % 256) + M * static_cast<int>(rank);  // this CTA's 64 keys within it
+  // Does query tile t have a stored block for key block kblk?
+  auto stored = [&](int t) {
+    int jlo, jn;
+    ws_key_blocks(t, N, p.causal, p.window, jlo, jn);
+    return kblk >= jlo && kblk < jlo + jn;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(BAR_FULL(s), 1);
+      mbar_init(BAR_EMPTY(s), 1);
+    }
+    mbar_init(BAR_FINAL, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmWS);
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    // ======================= TMA producer (both CTAs) =======================
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t cnt = 0;
+      auto acquire = [&](int& st) -> bool {
+        st = cnt % NST;
+        const uint32_t ph = (cnt / NST) & 1u;
+        if (!mbar_wait_cluster(BAR_EMPTY(st), ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_RING_EMPTY)) return false;
+        if (leader) mbar_arrive_expect_tx(BAR_FULL(st), 2 * C::STAGE_BYTES);
+        ++cnt;
+        return true;
+      };
+      const long long before_lo = ws_blocks_before(t_lo, N, p.causal, p.window);
+      for (int g0 = 0; g0 < G && ok; ++g0) {
+        const int hq = h * G + g0;
+        const long long head0 = (static_cast<long long>(b) * p.Hq + hq) * p.ws_bph;
+        long long before = before_lo;
+        for (int t = t_lo; t < t_hi && ok; ++t) {
+          int jlo, jn;
+          ws_key_blocks(t, N, p.causal, p.window, jlo, jn);
+          const long long blk = head0 + before + (kblk - jlo);
+          before += jn;
+          if (!(kblk >= jlo && kblk < jlo + jn)) continue;
+          int st;
+          // dS^T then P^T: 128 queries x this CTA's 64 keys of the block
+          ok = acquire(st);
+          if (!ok) break;
+          tma_load_3d_pair(smem_u32(sRing + st * C::STAGE_BYTES), &tmWS, mapa_shared(BAR_FULL(st), 0), kcol, 0,
+                           static_cast<int>(p.ws_blocks + blk));
+          ok = acquire(st);
+          if (!ok) break;
+          tma_load_3d_pair(smem_u32(sRing + st * C::STAGE_BYTES), &tmWS, mapa_shared(BAR_FULL(st), 0), kcol, 0,
+                           static_cast<int>(blk));
+          for (int g = 0; g < C::NACC && ok; ++g) {
+            for (int m = 0; m < 2 && ok; ++m) {
+              const CUtensorMap* map = (m == 0) ? &tmQ : &tmDO;
+              for (int j = 0; j < 2; ++j) {
+                ok = acquire(st);
+                if (!ok) break;
+                tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES), map, mapa_shared(BAR_FULL(st), 0),
+                                 64 * (4 * g + 2 * static_cast<int>(rank) + j), 128 * t, hq, b);
+              }
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ======================= MMA issuer (leader CTA only) =======================
+    if (leader && lane == 0) {
+      bool ok = true;
+      uint32_t cnt = 0;
+      bool first = true;
+      const uint64_t dRing = sw128_desc(smem_u32(sRing), C::STAGE_BYTES, 1024);
+      auto full = [&](uint32_t c) {
+        return mbar_wait_cluster(BAR_FULL(c % NST), (c / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL);
+      };
+      auto sdesc = [&](uint32_t c) { return dRing + static_cast<uint64_t>(((c % NST) * C::STAGE_BYTES) >> 4); };
+      for (int g0 = 0; g0 < G && ok; ++g0) {
+        for (int t = t_lo; t < t_hi && ok; ++t) {
+          if (!stored(t)) continue;
+          const uint32_t cA = cnt;  // dS^T at cA, P^T at cA + 1
+          ok = full(cA) && full(cA + 1);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t aDS = sdesc(cA), aP = sdesc(cA + 1);
+#pragma unroll 1
+          for (int g = 0; g < C::NACC && ok; ++g) {
+#pragma unroll 1
+            for (int m = 0; m < 2; ++m) {
+              const uint32_t c2 = cA + 2 + 4 * g + 2 * m;
+              ok = full(c2) && full(c2 + 1);
+              if (!ok) break;
+              tc_fence_after();
+              const uint64_t a = (m == 0) ? aDS : aP;
+              const uint64_t yb = sdesc(c2);
+              const uint32_t acc = (m == 0 ? 0u : 256u) + 128u * g;
+#pragma unroll
+              for (int tt = 0; tt < 8; ++tt) {
+                const uint64_t off = static_cast<uint64_t>((tt * 2048) >> 4);
+                mma_ss_pair(tbase + acc, a + off, yb + off, C::IDESC, (first && tt == 0) ? 0u : 1u);
+              }
+              mma_commit_pair(BAR_EMPTY(c2 % NST));
+              mma_commit_pair(BAR_EMPTY((c2 + 1) % NST));
+            }
+          }
+          if (!ok) break;
+          first = false;
+          mma_commit_pair(BAR_EMPTY(cA % NST));
+          mma_commit_pair(BAR_EMPTY((cA + 1) % NST));
+          cnt += C::SUB_STAGES;
+        }
+      }
+      if (ok) mma_commit_pair(BAR_FINAL);
+    }
+  } else if (warp >= 4) {
+    // ======================= epilogue warps (both CTAs) =======================
+    const int q4 = warp & 3;
+    const int half = q4 >> 1;
+    const int row = 32 * (q4 & 1) + lane;
+    const uint32_t tq = tbase + (static_cast<uint32_t>(q4 * 32) << 16);
+    bool any = false;
+    for (int t = t_lo; t < t_hi && !any; ++t) any = stored(t);
+    bool ok = true;
+    if (any) {
+      ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) tc_fence_after();
+    }
+    const int orow = r0 + row;
+    // tcgen05.ld is warp-collective: every lane loads, only live rows store.
+    if (ok) {
+#pragma unroll 1
+      for (int m = 0; m < 2; ++m) {
+        void* out = (m == 0) ? p.out : p.out2;
+        const long long obase = (m == 0)
+                                    ? static_cast<long long>(b) * p.out_sb + static_cast<long long>(h) * p.out_sh +
+                                          static_cast<long long>(orow) * p.out_sn
+                                    : static_cast<long long>(b) * p.out2_sb + static_cast<long long>(h) * p.out2_sh +
+                                          static_cast<long long>(orow) * p.out2_sn;
+        const float mul = (m == 0) ? p.scale : 1.f;
+#pragma unroll 1
+        for (int g = 0; g < C::NACC; ++g) {
+#pragma unroll 1
+          for (int k = 0; k < 4; ++k) {
+            float v[32];
+            if (any) {
+              uint32_t r[32];
+              tmem_ld32(tq + 256 * m + g * 128 + 32 * k, r);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * mul;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            }
+            if (orow < N) store_row32<C::BF16>(out, obase + 256 * g + 128 * half + 32 * k, v);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, 512);
+  }
+}
+
+}  // namespace gqafa

@@ -59,6 +59,16 @@ struct KParams {
   const void* dout;
   long long do_sb, do_sh, do_sn;
   int* status;
+  // Materialised backward (head_dim 512): the dQ kernel also writes P and dS
+  // into `ws` when it is non-null; the dK/dV kernel reads them back and
+  // writes dK to `out` and dV to `out2`. Layout: ws_blocks blocks of P, then
+  // ws_blocks blocks of dS; block (b, h, q tile t, key block j) holds
+  // [128 queries][256 keys] 16-bit values, row-major, at index
+  // (b * Hq + h) * ws_bph + ws_blocks_before(t) + (j - first key block of t).
+  void* ws;
+  long long ws_bph, ws_blocks;
+  void* out2;
+  long long out2_sb, out2_sh, out2_sn;
   // Optional diagnostics: when non-null, each CTA adds the cycles its roles
   // spend waiting (see WaitCounter) into these counters. Null on the hot path.
   unsigned long long* prof;
@@ -77,6 +87,33 @@ enum WaitCounter : int {
   WC_CTAS = 8,            // number of CTAs that reported
   WC_NUM = 9
 };
+
+// Key blocks (256 keys each) that query tile t (rows 128t .. 128t+127)
+// attends: [jlo, jlo + jn). Same ranges as the head_dim-512 dQ kernel's items.
+__host__ __device__ __forceinline__ void ws_key_blocks(int t, int N, int causal, int window, int& jlo, int& jn) {
+  const int kv_hi = causal ? min(N, 128 * t + 128) : N;
+  const int kv_lo = (causal && window > 0) ? max(0, 128 * t - window + 1) : 0;
+  jlo = kv_lo / 256;
+  jn = (kv_hi + 255) / 256 - jlo;
+}
+
+// Blocks stored for query tiles 0 .. t-1 of one head (t <= number of tiles).
+__host__ __device__ inline long long ws_blocks_before(int t, int N, int causal, int window) {
+  const int T = (N + 127) / 128;
+  if (!causal) return static_cast<long long>(t) * ((N + 255) / 256);
+  if (window == 0 && t <= T - 1) {
+    // tiles t' < t <= T-1 end before N: tile t' has ceil((t'+1)/2) blocks
+    const long long h = t / 2;
+    return (t % 2 == 0) ? h * (h + 1) : (h + 1) * (h + 1);
+  }
+  long long n = 0;
+  for (int u = 0; u < t; ++u) {
+    int jlo, jn;
+    ws_key_blocks(u, N, causal, window, jlo, jn);
+    n += jn;
+  }
+  return n;
+}
 
 template <int ROLE_, int M_, int D_, int DC_, int BN_, int NS_, int NSTAGES_, int YGROUP_, bool BF16_>
 struct Cfg {

@@ -75,7 +75,8 @@ template <class C>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tmR1, const __grid_constant__ CUtensorMap tmR2,
                      const __grid_constant__ CUtensorMap tmC1, const __grid_constant__ CUtensorMap tmC2,
-                     const __grid_constant__ CUtensorMap tmY, const KParams p) {
+                     const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmWS,
+                     const KParams p) {
   constexpr int M = C::M, MP = C::MP, BN = C::BN, NS = C::NS, NST = C::NSTAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -387,6 +388,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     }
 
     constexpr int KCH = C::SBUF_COLS / 32;  // 32-column chunks this thread owns per item
+    // Materialised backward (dQ role): workspace block of item 0 of this
+    // (b, h, q tile); item i is block ws_blk0 + i, its dS block ws_blocks later.
+    long long ws_blk0 = 0;
+    if constexpr (C::ROLE == ROLE_DQ) {
+      if (p.ws != nullptr)
+        ws_blk0 = (static_cast<long long>(b) * p.Hq + h) * p.ws_bph + ws_blocks_before(tile, N, p.causal, p.window);
+    }
     if constexpr (C::ROLE == ROLE_FWD) {
       // Online softmax (exp2 domain, lazy rescaling as in attn_kernel.cuh) over
       // the BN/2 columns of every item this thread holds. The two warps holding
@@ -544,7 +552,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       }
       tock(WC_ROW_EPILOGUE, t_epi);
     } else {
-      for (int i = 0; i < n_items && ok; ++i) {
+      // Materialised backward (dQ role with a workspace): P and then dS of
+      // every item pass through the P buffer, from which TMA stores them to
+      // the workspace as one [64 rows x 256] block slice per CTA. The four row
+      // warps synchronise on a named barrier around each store, so no warp
+      // leaves the loop early: after a failed wait a warp skips its work but
+      // still reaches every barrier.
+      const bool ws_on = (C::ROLE == ROLE_DQ && BN == 256) && p.ws != nullptr;
+      const bool tid0 = (warp == 4 && lane == 0);
+      auto row_bar = [&]() { asm volatile("bar.sync 1, 128;" ::: "memory"); };
+      // K-major SWIZZLE_128B [64 rows x BN] tile of 64-column panels.
+      auto put = [&](int sb, int k, const float (&vals)[32]) {
+        const int col = half * (BN / 2) + 32 * k;  // column within the item
+        uint8_t* prow = sP + sb * C::PBUF_ONE + (col / 64) * (M * 128) + row * 128;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int chunk16 = (col % 64) / 8 + cc;
+          uint4 w;
+          w.x = pack2<C::BF16>(vals[8 * cc + 0], vals[8 * cc + 1]);
+          w.y = pack2<C::BF16>(vals[8 * cc + 2], vals[8 * cc + 3]);
+          w.z = pack2<C::BF16>(vals[8 * cc + 4], vals[8 * cc + 5]);
+          w.w = pack2<C::BF16>(vals[8 * cc + 6], vals[8 * cc + 7]);
+          *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (row & 7)) * 16)) = w;
+        }
+      };
+      auto store_block = [&](int sb, long long blk) {
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c)
+          tma_store_3d(&tmWS, smem_u32(sP + sb * C::PBUF_ONE + c * (M * 128)), 64 * c, M * static_cast<int>(rank),
+                       static_cast<int>(blk));
+        bulk_commit();
+      };
+      for (int i = 0; i < n_items; ++i) {
         const int sb = i % NS;
         const int c0 = item_col0(i);
         const int cb = c0 + half * (BN / 2);  // first column this thread owns
@@ -563,89 +602,105 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         }
         const long long t_w = tick();
         // dQ / dK: wait for S only; dP is waited for after P is computed.
-        ok = mbar_wait_cluster(C::HAS_DP ? BAR_SREADY(sb) : BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status,
-                               ST_TIMEOUT_SCORES);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
+        if (ok) {
+          ok = mbar_wait_cluster(C::HAS_DP ? BAR_SREADY(sb) : BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status,
+                                 ST_TIMEOUT_SCORES);
+          ok = __all_sync(0xffffffffu, ok);
+        }
         tock(WC_ROW_SFULL, t_w);
         const long long t_work = tick();
-        tc_fence_after();
-        int lo_abs, hi_abs;
-        attended_interval(C::ROWS_ARE_Q, r0 + row, N, p.causal, p.window, lo_abs, hi_abs);
-        const int lo_rel = lo_abs - cb;
-        const unsigned span = span_of(lo_rel, hi_abs - cb);
         const uint32_t s_col = C::ACC_COLS + sb * C::SBUF_COLS;
         const uint32_t dp_col = C::ACC_COLS + (NS + sb) * C::SBUF_COLS;
         constexpr int KB = KCH < 2 ? KCH : 2;  // chunks loaded per TMEM round trip (register budget)
         // P = exp2(S * scale * log2 e - lse * log2 e), masked, for all columns this thread owns.
         float pv[KCH][32];
-#pragma unroll
-        for (int kb = 0; kb < KCH; kb += KB) {
-          uint32_t rs[KB][32];
-#pragma unroll
-          for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + s_col + 32 * (kb + u), rs[u]);
-#pragma unroll
-          for (int u = 0; u < KB; ++u) tmem_ld_wait32(rs[u]);
-#pragma unroll
-          for (int u = 0; u < KB; ++u) {
-            const int k = kb + u;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float l2 = C::ROWS_ARE_Q ? row_lse2 : __shfl_sync(0xffffffffu, col_lse2[k], j);
-              const float e = ex2(__uint_as_float(rs[u][j]) * sl2 - l2);
-              pv[k][j] = (static_cast<unsigned>(32 * k + j - lo_rel) < span) ? e : 0.f;
-            }
-          }
-        }
-        if constexpr (C::HAS_DP) {
-          ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
+        if (ok) {
           tc_fence_after();
-        }
+          int lo_abs, hi_abs;
+          attended_interval(C::ROWS_ARE_Q, r0 + row, N, p.causal, p.window, lo_abs, hi_abs);
+          const int lo_rel = lo_abs - cb;
+          const unsigned span = span_of(lo_rel, hi_abs - cb);
 #pragma unroll
-        for (int kb = 0; kb < KCH; kb += KB) {
-          uint32_t rd[KB][32];
-          if constexpr (C::HAS_DP) {
+          for (int kb = 0; kb < KCH; kb += KB) {
+            uint32_t rs[KB][32];
 #pragma unroll
-            for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + dp_col + 32 * (kb + u), rd[u]);
+            for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + s_col + 32 * (kb + u), rs[u]);
 #pragma unroll
-            for (int u = 0; u < KB; ++u) tmem_ld_wait32(rd[u]);
-          }
+            for (int u = 0; u < KB; ++u) tmem_ld_wait32(rs[u]);
 #pragma unroll
-          for (int u = 0; u < KB; ++u) {
-            const int k = kb + u;
-            float v[32];
+            for (int u = 0; u < KB; ++u) {
+              const int k = kb + u;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if constexpr (C::HAS_DP) {
-                const float dl = C::ROWS_ARE_Q ? row_delta : __shfl_sync(0xffffffffu, col_delta[k], j);
-                v[j] = pv[k][j] * (__uint_as_float(rd[u][j]) - dl);
-              } else {
-                v[j] = pv[k][j];
+              for (int j = 0; j < 32; ++j) {
+                const float l2 = C::ROWS_ARE_Q ? row_lse2 : __shfl_sync(0xffffffffu, col_lse2[k], j);
+                const float e = ex2(__uint_as_float(rs[u][j]) * sl2 - l2);
+                pv[k][j] = (static_cast<unsigned>(32 * k + j - lo_rel) < span) ? e : 0.f;
               }
             }
-            // K-major SWIZZLE_128B [64 rows x BN] tile of 64-column panels.
-            const int col = half * (BN / 2) + 32 * k;  // column within the item
-            uint8_t* prow = sP + sb * C::PBUF_ONE + (col / 64) * (M * 128) + row * 128;
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-              const int chunk16 = (col % 64) / 8 + cc;
-              uint4 w;
-              w.x = pack2<C::BF16>(v[8 * cc + 0], v[8 * cc + 1]);
-              w.y = pack2<C::BF16>(v[8 * cc + 2], v[8 * cc + 3]);
-              w.z = pack2<C::BF16>(v[8 * cc + 4], v[8 * cc + 5]);
-              w.w = pack2<C::BF16>(v[8 * cc + 6], v[8 * cc + 7]);
-              *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (row & 7)) * 16)) = w;
-            }
           }
         }
-        tc_fence_before();
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_remote(pready_l0 + 8u * sb);
+        if (ws_on) {
+          // P -> buffer -> workspace. The previous item's dS store must have
+          // finished reading the buffer; its MMAs have (S-ready implies it).
+          if (tid0) bulk_wait_read0();
+          row_bar();
+          if (ok) {
+#pragma unroll
+            for (int k = 0; k < KCH; ++k) put(sb, k, pv[k]);
+            fence_proxy_async_smem();
+          }
+          row_bar();
+          if (tid0 && ok) store_block(sb, ws_blk0 + i);
+        }
+        if (C::HAS_DP && ok) {
+          ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) tc_fence_after();
+        }
+        if (ws_on) {
+          if (tid0) bulk_wait_read0();  // the P store has read the buffer
+          row_bar();
+        }
+        if (ok) {
+#pragma unroll
+          for (int kb = 0; kb < KCH; kb += KB) {
+            uint32_t rd[KB][32];
+            if constexpr (C::HAS_DP) {
+#pragma unroll
+              for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + dp_col + 32 * (kb + u), rd[u]);
+#pragma unroll
+              for (int u = 0; u < KB; ++u) tmem_ld_wait32(rd[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < KB; ++u) {
+              const int k = kb + u;
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if constexpr (C::HAS_DP) {
+                  const float dl = C::ROWS_ARE_Q ? row_delta : __shfl_sync(0xffffffffu, col_delta[k], j);
+                  v[j] = pv[k][j] * (__uint_as_float(rd[u][j]) - dl);
+                } else {
+                  v[j] = pv[k][j];
+                }
+              }
+              put(sb, k, v);
+            }
+          }
+          tc_fence_before();
+          fence_proxy_async_smem();
+        }
+        if (ws_on) {
+          row_bar();
+          if (tid0 && ok) store_block(sb, p.ws_blocks + ws_blk0 + i);
+        }
+        if (ok) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(pready_l0 + 8u * sb);
+        }
         tock(WC_ROW_WORK, t_work);
       }
+      if (ws_on && tid0) bulk_wait0();  // workspace writes complete before the CTA exits
 
       // ---------------- epilogue ----------------
       const long long t_epi = tick();

@@ -19,6 +19,7 @@
 
 #include "../../include/gqa_fa_b200.h"
 #include "attn_pair_kernel.cuh"
+#include "attn_dkv_kernel.cuh"
 
 namespace gqafa {
 
@@ -139,7 +140,9 @@ int* status_ptr() {
 }
 
 template <class C>
-int launch(const CUtensorMap (&maps)[5], KParams p, cudaStream_t stream) {
+// maps: R1, R2, C1, C2, Y and (pair kernels) the workspace store map; an
+// unused slot may hold any valid map.
+int launch(const CUtensorMap (&maps)[6], KParams p, cudaStream_t stream) {
   static std::atomic<unsigned long long> attr_done_mask{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(GQAFA_ERR_CUDA, "cudaGetDevice failed");
@@ -165,7 +168,7 @@ int launch(const CUtensorMap (&maps)[5], KParams p, cudaStream_t stream) {
   if (grid <= 0 || grid > 0x7fffffffLL) return fail(GQAFA_ERR_INVALID, "grid size %lld out of range", grid);
   if constexpr (C::PAIR) {
     attn_pair_kernel<C><<<(unsigned)grid, 256, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3],
-                                                                         maps[4], p);
+                                                                         maps[4], maps[5], p);
   } else {
     attn_kernel<C><<<(unsigned)grid, 256, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], p);
   }
@@ -187,6 +190,8 @@ template <bool BF16> using Fwd512 = PairCfg<ROLE_FWD, 512, 256, 2, 6, BF16>;
 template <bool BF16> using Dq512 = PairCfg<ROLE_DQ, 512, 256, 1, 4, BF16>;
 template <bool BF16> using Dk512 = PairCfg<ROLE_DK, 512, 256, 1, 4, BF16>;
 template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 256, 2, 6, BF16>;
+
+template <bool BF16> using Dkv512 = DkvCfg<512, 14, BF16>;
 
 struct Problem {
   int B, Hq, Hkv, N, D, causal, window;
@@ -250,7 +255,7 @@ void set_out(KParams& p, void* ptr, const TensorDesc& t) {
 template <bool BF16, class CF>
 int fwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const TensorDesc& v, void* o,
              const TensorDesc& od, float* lse, cudaStream_t st) {
-  CUtensorMap maps[5];
+  CUtensorMap maps[6];
   int rc;
   if ((rc = encode_map(&maps[0], q, pr.B, pr.N, pr.D, CF::M, BF16))) return rc;
   int cbox = CF::BN, ybox = CF::BN;
@@ -267,6 +272,7 @@ int fwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
   p.lse = lse;
   p.status = status_ptr();
   if (!p.status) return fail(GQAFA_ERR_CUDA, "cannot resolve the device status word");
+  maps[5] = maps[0];
   return launch<CF>(maps, p, st);
 }
 
@@ -279,7 +285,7 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
   if (!status) return fail(GQAFA_ERR_CUDA, "cannot resolve the device status word");
   int rc;
   if (stages & 1) {  // dQ + delta
-    CUtensorMap maps[5];
+    CUtensorMap maps[6];
     if ((rc = encode_map(&maps[0], q, pr.B, pr.N, pr.D, CQ::M, BF16))) return rc;
     if ((rc = encode_map(&maps[1], dout, pr.B, pr.N, pr.D, CQ::M, BF16))) return rc;
     if ((rc = encode_map(&maps[2], k, pr.B, pr.N, pr.D, CQ::C_BOX, BF16))) return rc;
@@ -298,10 +304,11 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
     p.do_sh = dout.sh;
     p.do_sn = dout.sn;
     p.status = status;
+    if (!p.ws) maps[5] = maps[0];
     if ((rc = launch<CQ>(maps, p, st))) return rc;
   }
   if (stages & 2) {  // dK
-    CUtensorMap maps[5];
+    CUtensorMap maps[6];
     if ((rc = encode_map(&maps[0], k, pr.B, pr.N, pr.D, CK::M, BF16))) return rc;
     if ((rc = encode_map(&maps[1], v, pr.B, pr.N, pr.D, CK::M, BF16))) return rc;
     if ((rc = encode_map(&maps[2], q, pr.B, pr.N, pr.D, CK::C_BOX, BF16))) return rc;
@@ -312,10 +319,11 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
     p.lse = const_cast<float*>(lse);
     p.delta = delta;
     p.status = status;
+    maps[5] = maps[0];
     if ((rc = launch<CK>(maps, p, st))) return rc;
   }
   if (stages & 4) {  // dV
-    CUtensorMap maps[5];
+    CUtensorMap maps[6];
     if ((rc = encode_map(&maps[0], k, pr.B, pr.N, pr.D, CV::M, BF16))) return rc;
     if ((rc = encode_map(&maps[2], q, pr.B, pr.N, pr.D, CV::C_BOX, BF16))) return rc;
     if ((rc = encode_map(&maps[4], dout, pr.B, pr.N, pr.D, CV::Y_BOX, BF16))) return rc;
@@ -326,7 +334,115 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
     p.lse = const_cast<float*>(lse);
     p.delta = delta;
     p.status = status;
+    maps[5] = maps[0];
     if ((rc = launch<CV>(maps, p, st))) return rc;
+  }
+  return GQAFA_OK;
+}
+
+// The materialised backward's workspace as 2 * nblk blocks of [128 queries][256
+// keys], 16-bit; boxes of 64 keys x box_rows queries, 128-byte swizzle.
+int encode_ws_map(CUtensorMap* m, void* ws, long long nblk, int box_rows, bool bf16) {
+  EncodeFn enc = get_encode();
+  if (!enc) return fail(GQAFA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t dims[3] = {256u, 128u, (cuuint64_t)(2 * nblk)};
+  cuuint64_t strides[2] = {256u * 2u, 128u * 256u * 2u};
+  cuuint32_t box[3] = {64u, (cuuint32_t)box_rows, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ws, dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GQAFA_ERR_CUDA, "cuTensorMapEncodeTiled (workspace) failed (%d)", (int)r);
+  return GQAFA_OK;
+}
+
+// Blocks of P (and as many of dS) one head stores in the materialised backward.
+long long ws_blocks_per_head(const Problem& pr) {
+  const int T = (pr.N + 127) / 128;
+  int jlo, jn;
+  ws_key_blocks(T - 1, pr.N, pr.causal, pr.window, jlo, jn);
+  return ws_blocks_before(T - 1, pr.N, pr.causal, pr.window) + jn;
+}
+
+long long ws_bytes(const Problem& pr) {
+  if (pr.D != 512) return 0;
+  return 2LL * pr.B * pr.Hq * ws_blocks_per_head(pr) * (128LL * 256 * 2);
+}
+
+// Materialised head_dim-512 backward: stage bit 1 = dQ + delta, writing P and
+// dS to the workspace; bit 2 = dK and dV from them.
+template <bool BF16>
+int bwd_ws_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const TensorDesc& v,
+                const TensorDesc& o, const TensorDesc& dout, const float* lse, void* dq, const TensorDesc& dqd,
+                void* dk, const TensorDesc& dkd, void* dv, const TensorDesc& dvd, float* delta, void* ws,
+                cudaStream_t st, int stages) {
+  using CQ = Dq512<BF16>;
+  using CKV = Dkv512<BF16>;
+  int* status = status_ptr();
+  if (!status) return fail(GQAFA_ERR_CUDA, "cannot resolve the device status word");
+  const long long bph = ws_blocks_per_head(pr);
+  const long long nblk = static_cast<long long>(pr.B) * pr.Hq * bph;
+  if (2 * nblk > 0x7fffffffLL) return fail(GQAFA_ERR_INVALID, "workspace block count out of range");
+  int rc;
+  if (stages & 1) {
+    CUtensorMap maps[6];
+    if ((rc = encode_map(&maps[0], q, pr.B, pr.N, pr.D, CQ::M, BF16))) return rc;
+    if ((rc = encode_map(&maps[1], dout, pr.B, pr.N, pr.D, CQ::M, BF16))) return rc;
+    if ((rc = encode_map(&maps[2], k, pr.B, pr.N, pr.D, CQ::C_BOX, BF16))) return rc;
+    if ((rc = encode_map(&maps[3], v, pr.B, pr.N, pr.D, CQ::C_BOX, BF16))) return rc;
+    if ((rc = encode_map(&maps[4], k, pr.B, pr.N, pr.D, CQ::Y_BOX, BF16))) return rc;
+    KParams p = base_params(pr);
+    set_out(p, dq, dqd);
+    p.lse = const_cast<float*>(lse);
+    p.delta = delta;
+    p.o = o.ptr;
+    p.o_sb = o.sb;
+    p.o_sh = o.sh;
+    p.o_sn = o.sn;
+    p.dout = dout.ptr;
+    p.do_sb = dout.sb;
+    p.do_sh = dout.sh;
+    p.do_sn = dout.sn;
+    p.ws = ws;
+    p.ws_bph = bph;
+    p.ws_blocks = nblk;
+    p.status = status;
+    if ((rc = encode_ws_map(&maps[5], ws, nblk, CQ::M, BF16))) return rc;
+    if ((rc = launch<CQ>(maps, p, st))) return rc;
+  }
+  if (stages & 2) {
+    CUtensorMap mws, mq, mdo;
+    if ((rc = encode_ws_map(&mws, ws, nblk, 128, BF16))) return rc;
+    if ((rc = encode_map(&mq, q, pr.B, pr.N, pr.D, CKV::Y_BOX, BF16))) return rc;
+    if ((rc = encode_map(&mdo, dout, pr.B, pr.N, pr.D, CKV::Y_BOX, BF16))) return rc;
+    KParams p = base_params(pr);
+    set_out(p, dk, dkd);
+    p.out2 = dv;
+    p.out2_sb = dvd.sb;
+    p.out2_sh = dvd.sh;
+    p.out2_sn = dvd.sn;
+    p.ws = ws;
+    p.ws_bph = bph;
+    p.ws_blocks = nblk;
+    p.status = status;
+    p.tile_begin = 0;
+    p.num_row_tiles = (pr.N + CKV::MP - 1) / CKV::MP;
+    p.prof = nullptr;
+    static std::atomic<unsigned long long> attr_done_mask{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return fail(GQAFA_ERR_CUDA, "cudaGetDevice failed");
+    const unsigned long long bit = 1ULL << (dev & 63);
+    if (!(attr_done_mask.load() & bit)) {
+      cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&attn_dkv_kernel<CKV>),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, CKV::SMEM_BYTES);
+      if (e != cudaSuccess) return fail(GQAFA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      attr_done_mask.fetch_or(bit);
+    }
+    const long long grid = 2LL * p.num_row_tiles * pr.Hkv * pr.B;
+    if (grid > 0x7fffffffLL) return fail(GQAFA_ERR_INVALID, "grid size %lld out of range", grid);
+    attn_dkv_kernel<CKV><<<(unsigned)grid, 256, CKV::SMEM_BYTES, st>>>(mws, mq, mdo, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(GQAFA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
   }
   return GQAFA_OK;
 }
@@ -461,6 +577,57 @@ extern "C" int gqafa_bwd_stage_rows(int stage, GQAFA_BWD_PARAMS, int row_begin, 
     return GQAFA_ERR_INVALID;
   }
   return bwd_entry(1 << stage, row_begin, row_end, GQAFA_BWD_ARGS);
+}
+
+extern "C" long long gqafa_bwd_workspace_size(int batch, int heads_q, int heads_kv, int seqlen, int head_dim,
+                                              int causal, int window) {
+  g_last_error.clear();
+  Problem pr{};
+  if (check_problem(batch, heads_q, heads_kv, seqlen, head_dim, 1.f, causal, window, GQAFA_DTYPE_BF16, &pr))
+    return -1;
+  return ws_bytes(pr);
+}
+
+static int bwd_ws_entry(int stages, GQAFA_BWD_PARAMS, void* workspace, long long workspace_bytes) {
+  g_last_error.clear();
+  Problem pr{};
+  int rc;
+  if ((rc = check_problem(batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, window, dtype, &pr)))
+    return rc;
+  const long long need = ws_bytes(pr);
+  if (need == 0) return bwd_entry(stages == 2 ? 6 : (stages == 1 ? 1 : 7), 0, -1, GQAFA_BWD_ARGS);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(GQAFA_ERR_INVALID, "workspace of %lld bytes needed, got %lld", need, workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(GQAFA_ERR_INVALID, "workspace must be 256-byte aligned");
+  TensorDesc qd, kd, vd, od, dod, dqd, dkd, dvd;
+  if ((rc = check_tensor("q", q, q_strides, batch, heads_q, seqlen, head_dim, &qd))) return rc;
+  if ((rc = check_tensor("k", k, k_strides, batch, heads_kv, seqlen, head_dim, &kd))) return rc;
+  if ((rc = check_tensor("v", v, v_strides, batch, heads_kv, seqlen, head_dim, &vd))) return rc;
+  if ((rc = check_tensor("o", o, o_strides, batch, heads_q, seqlen, head_dim, &od))) return rc;
+  if ((rc = check_tensor("dout", dout, dout_strides, batch, heads_q, seqlen, head_dim, &dod))) return rc;
+  if ((rc = check_tensor("dq", dq, dq_strides, batch, heads_q, seqlen, head_dim, &dqd))) return rc;
+  if ((rc = check_tensor("dk", dk, dk_strides, batch, heads_kv, seqlen, head_dim, &dkd))) return rc;
+  if ((rc = check_tensor("dv", dv, dv_strides, batch, heads_kv, seqlen, head_dim, &dvd))) return rc;
+  if (lse == nullptr || delta == nullptr) return fail(GQAFA_ERR_INVALID, "lse and delta must be non-null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = bind_device(st))) return rc;
+  return pr.bf16 ? bwd_ws_impl<true>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk, dkd, dv, dvd, delta, workspace, st,
+                                     stages)
+                 : bwd_ws_impl<false>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk, dkd, dv, dvd, delta, workspace, st,
+                                      stages);
+}
+
+extern "C" int gqafa_bwd_ws(GQAFA_BWD_PARAMS, void* workspace, long long workspace_bytes) {
+  return bwd_ws_entry(3, GQAFA_BWD_ARGS, workspace, workspace_bytes);
+}
+
+extern "C" int gqafa_bwd_ws_stage(int stage, GQAFA_BWD_PARAMS, void* workspace, long long workspace_bytes) {
+  if (stage < 0 || stage > 1) {
+    g_last_error = "stage must be 0 (dQ + delta + P/dS) or 1 (dK + dV)";
+    return GQAFA_ERR_INVALID;
+  }
+  return bwd_ws_entry(1 << stage, GQAFA_BWD_ARGS, workspace, workspace_bytes);
 }
 
 // ---------------------------------------------------------------------------

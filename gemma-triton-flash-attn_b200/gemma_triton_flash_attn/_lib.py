@@ -28,6 +28,9 @@ EXPORTED_SYMBOLS = (
     "gqafa_bwd",
     "gqafa_bwd_stage",
     "gqafa_bwd_noalloc",
+    "gqafa_bwd_ws",
+    "gqafa_bwd_ws_stage",
+    "gqafa_bwd_workspace_size",
     "gqafa_fwd_rows",
     "gqafa_bwd_stage_rows",
     "gqafa_supported",
@@ -81,6 +84,13 @@ def load():
             + [_I, _I, _I, _I, _I, _F, _I, _I, _I, _P]
         )
         lib.gqafa_bwd_noalloc.restype = _I
+        _L = ctypes.c_longlong
+        lib.gqafa_bwd_ws.argtypes = lib.gqafa_bwd.argtypes + [_P, _L]
+        lib.gqafa_bwd_ws.restype = _I
+        lib.gqafa_bwd_ws_stage.argtypes = [_I] + lib.gqafa_bwd.argtypes + [_P, _L]
+        lib.gqafa_bwd_ws_stage.restype = _I
+        lib.gqafa_bwd_workspace_size.argtypes = [_I] * 7
+        lib.gqafa_bwd_workspace_size.restype = _L
         lib.gqafa_supported.argtypes = [_I, _I]
         lib.gqafa_supported.restype = _I
         lib.gqafa_last_error.argtypes = []

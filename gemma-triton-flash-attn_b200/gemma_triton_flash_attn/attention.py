@@ -30,6 +30,7 @@ Differences from the reference, all deliberate:
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -198,11 +199,44 @@ def _fwd(q, k, v, causal, window, scale, want_lse, rows=None, out=None):
     return o, lse
 
 
-def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=None):
+def _workspace_limit():
+    """Largest backward workspace (bytes) `_bwd` may allocate; GQAFA_BWD_WORKSPACE_LIMIT
+    overrides (0 turns the materialised backward off). Default: no limit beyond
+    what the allocator can give; an allocation failure falls back to the
+    recomputing backward."""
+    env = os.environ.get("GQAFA_BWD_WORKSPACE_LIMIT")
+    return None if env is None else int(env)
+
+
+def bwd_workspace_size(b, h_q, h_kv, n, d, causal, window):
+    """Bytes of workspace the materialised backward needs (0: not applicable)."""
+    size = _lib.load().gqafa_bwd_workspace_size(b, h_q, h_kv, n, d, 1 if causal else 0, int(window))
+    if size < 0:
+        _lib.check(_lib.GQAFA_ERR_INVALID)
+    return int(size)
+
+
+def _alloc_workspace(size, device):
+    limit = _workspace_limit()
+    if size <= 0 or (limit is not None and size > limit):
+        return None
+    try:
+        return torch.empty(size, dtype=torch.uint8, device=device)
+    except torch.cuda.OutOfMemoryError:
+        return None
+
+
+def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=None, workspace=None):
     """Backward launches. `stage` (0 dQ+delta, 1 dK, 2 dV) runs one kernel only,
     into the buffers of `out` = (dq, dk, dv, delta) (profiling / benchmarks);
     with `rows` = (begin, end) only those rows (query rows for stage 0, key rows
-    for stages 1 and 2)."""
+    for stages 1 and 2).
+
+    A full backward (no stage, no rows) at head_dim 512 takes the materialised
+    path (gqafa_bwd_ws: the dQ kernel stores P and dS, one kernel makes dK and
+    dV from them) with a workspace from the caching allocator, or `workspace`
+    when given; without the memory it runs the recomputing gqafa_bwd. With a
+    `workspace` tensor, `stage` 0 / 1 selects that path's kernels instead."""
     lib = _lib.load()
     b, h_q, n, d = q.shape
     h_kv = k.shape[1]
@@ -215,7 +249,16 @@ def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=
         delta = torch.empty((b, h_q, n), dtype=torch.float32, device=q.device)
     else:
         dq, dk, dv, delta = out
-    if rows is not None:
+    ws = workspace
+    if ws is None and stage is None and rows is None:
+        ws = _alloc_workspace(bwd_workspace_size(b, h_q, h_kv, n, d, causal, window), q.device)
+    if ws is not None:
+        tail = (ws.data_ptr(), ws.numel() * ws.element_size())
+        if stage is None:
+            fn = lambda *a: lib.gqafa_bwd_ws(*a, *tail)  # noqa: E731
+        else:
+            fn = lambda *a: lib.gqafa_bwd_ws_stage(int(stage), *a, *tail)  # noqa: E731
+    elif rows is not None:
         fn = lambda *a: lib.gqafa_bwd_stage_rows(int(stage), *a, int(rows[0]), int(rows[1]))  # noqa: E731
     else:
         fn = lib.gqafa_bwd if stage is None else (lambda *a: lib.gqafa_bwd_stage(int(stage), *a))

@@ -104,6 +104,38 @@ GQAFA_API int gqafa_bwd_noalloc(const void* q, const long long* q_strides, const
                                 int head_dim, float softmax_scale, int causal, int window, int dtype,
                                 void* stream);
 
+/* Materialised backward (head_dim 512). The reference's dK/dV launch
+ * recomputes S = Q K^T and dP = dO V^T for every (key tile, query block)
+ * (flash_attn/attention.py:1602-1620) after its dQ launch already computed
+ * them (flash_attn/attention.py:1506-1523). gqafa_bwd_ws instead has the dQ
+ * kernel also write P and dS (16-bit, the attended 128 x 256 blocks only) to a
+ * caller-provided workspace and computes dK and dV from them in one kernel:
+ * 10 instead of 16 head_dim-sized MACs per attended (query, key) pair.
+ * Same arguments and results as gqafa_bwd, plus the workspace (256-byte
+ * aligned device memory, any contents). gqafa_bwd_workspace_size returns the
+ * bytes it needs (2 * B * H_Q * blocks * 64 KiB), 0 where the materialised
+ * path does not apply (head_dim 256: gqafa_bwd_ws then runs gqafa_bwd and
+ * ignores the workspace), or -1 for invalid sizes. */
+GQAFA_API long long gqafa_bwd_workspace_size(int batch, int heads_q, int heads_kv, int seqlen, int head_dim,
+                                             int causal, int window);
+GQAFA_API int gqafa_bwd_ws(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+                           const void* v, const long long* v_strides, const void* o, const long long* o_strides,
+                           const void* dout, const long long* dout_strides, const float* lse, void* dq,
+                           const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
+                           const long long* dv_strides, float* delta, int batch, int heads_q, int heads_kv,
+                           int seqlen, int head_dim, float softmax_scale, int causal, int window, int dtype,
+                           void* stream, void* workspace, long long workspace_bytes);
+/* One kernel of gqafa_bwd_ws: stage 0 = dQ + delta + P/dS, 1 = dK + dV
+ * (needs stage 0's workspace contents). For per-kernel timing. */
+GQAFA_API int gqafa_bwd_ws_stage(int stage, const void* q, const long long* q_strides, const void* k,
+                                 const long long* k_strides, const void* v, const long long* v_strides,
+                                 const void* o, const long long* o_strides, const void* dout,
+                                 const long long* dout_strides, const float* lse, void* dq,
+                                 const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
+                                 const long long* dv_strides, float* delta, int batch, int heads_q, int heads_kv,
+                                 int seqlen, int head_dim, float softmax_scale, int causal, int window, int dtype,
+                                 void* stream, void* workspace, long long workspace_bytes);
+
 /* Row-range variants for splitting one (batch, KV-group) unit across GPUs
  * by sequence blocks (no counterpart in the reference, whose launches always
  * cover every row). Same arguments as gqafa_fwd / gqafa_bwd_stage plus

@@ -88,3 +88,25 @@ def test_bwd_validation_requires_lse_and_delta():
                        1, 8, 8, 64, 256, 0.0625, 1, 0, 0, None)
     assert rc == _lib.GQAFA_ERR_INVALID
     assert "lse and delta" in lib.gqafa_last_error().decode()
+
+
+def _blocks_per_head(n, causal, window):
+    """Attended (128-query tile, 256-key block) pairs of one head, counted directly."""
+    total = 0
+    for t in range((n + 127) // 128):
+        hi = min(n, 128 * t + 128) if causal else n
+        lo = max(0, 128 * t - window + 1) if (causal and window) else 0
+        total += (hi + 255) // 256 - lo // 256
+    return total
+
+
+@pytest.mark.parametrize("n,causal,window", [(16384, True, 0), (300, True, 0), (129, True, 0), (200, False, 0),
+                                             (1000, True, 300), (777, True, 129), (64, False, 0),
+                                             (5000, True, 5000), (4096, True, 1)])
+def test_bwd_workspace_size(n, causal, window):
+    lib = _lib.load()
+    w = window if (causal and 0 < window < n) else 0
+    want = 2 * 2 * 8 * _blocks_per_head(n, causal, w) * 128 * 256 * 2
+    assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 512, int(causal), window) == want
+    assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 256, int(causal), window) == 0
+    assert lib.gqafa_bwd_workspace_size(2, 8, 3, n, 512, int(causal), window) == -1

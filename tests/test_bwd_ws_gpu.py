@@ -1,0 +1,99 @@
+"""The materialised head_dim-512 backward (gqafa_bwd_ws: the dQ kernel stores P
+and dS, one kernel computes dK and dV from them) against the fp32 reference and
+against the recomputing backward (gqafa_bwd), on causal, sliding-window,
+non-causal, ragged and GQA shapes."""
+import math
+
+import pytest
+import torch
+
+from gemma_triton_flash_attn import _lib
+from gemma_triton_flash_attn.attention import _bwd, _fwd, bwd_workspace_size
+from helpers import assert_close, make_inputs, torch_ref
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+CASES = [
+    # (B, Hq, Hkv, N, causal, window, dtype)
+    (1, 4, 1, 300, True, 0, torch.bfloat16),
+    (2, 4, 2, 200, False, 0, torch.float16),
+    (1, 2, 1, 1000, True, 300, torch.bfloat16),
+    (1, 4, 2, 777, True, 129, torch.float16),
+    (1, 8, 2, 2048, True, 0, torch.bfloat16),
+    (1, 2, 2, 129, True, 0, torch.bfloat16),
+    (1, 2, 1, 64, False, 0, torch.bfloat16),
+]
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    yield
+    assert _lib.device_status(torch.cuda.current_device(), reset=True) == 0, "a kernel wait timed out"
+
+
+def _run(B, Hq, Hkv, N, causal, window, dt, seed=0):
+    D = 512
+    q, k, v, do = (t.to(DEV) for t in make_inputs(B, Hq, Hkv, N, D, dtype=dt, factor=0.5, seed=seed))
+    scale = 1.0 / math.sqrt(D)
+    o, lse = _fwd(q, k, v, causal, window, scale, True)
+    size = bwd_workspace_size(B, Hq, Hkv, N, D, causal, window)
+    assert size > 0
+    # garbage in the workspace must not matter: every read block is written first
+    ws = torch.full((size,), 0xFF, dtype=torch.uint8, device=DEV)
+    got = _bwd(q, k, v, o, lse, do, causal, window, scale, workspace=ws)
+    # the recomputing kernels one stage at a time; dK (stage 1) reads the
+    # delta stage 0 wrote, so all stages share one buffer set
+    bufs = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty(B, Hq, N, device=DEV))
+    for s in range(3):
+        _bwd(q, k, v, o, lse, do, causal, window, scale, stage=s, out=bufs)
+    rec = bufs[:3]
+    torch.cuda.synchronize()
+    return (q, k, v, do, scale), got, rec
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"B{c[0]}H{c[1]}x{c[2]}N{c[3]}c{int(c[4])}w{c[5]}")
+def test_ws_matches_reference(case):
+    B, Hq, Hkv, N, causal, window, dt = case
+    (q, k, v, do, scale), got, rec = _run(*case)
+    ref = torch_ref(q, k, v, do, causal, window, scale)
+    emu = torch_ref(q, k, v, do, causal, window, scale, emulate=True)
+    mag = torch_ref(q, k, v, do, causal, window, scale, magnitudes=True)
+    for i, name in ((2, "dQ"), (3, "dK"), (4, "dV")):
+        assert_close(f"ws {case} {name}", got[i - 2], ref[i], emulated=emu[i], magnitude=mag[i])
+    # same math as the recomputing kernels; only fp32 summation order differs
+    for i, name in enumerate(("dQ", "dK", "dV")):
+        a, r = got[i].float(), rec[i].float()
+        assert (a - r).abs().max().item() <= 2e-2 * max(1.0, r.abs().max().item()), name
+
+
+def test_ws_dq_identical_to_recompute():
+    """The dQ kernel's result does not depend on whether it also stores P / dS."""
+    (_, got, rec) = _run(1, 4, 1, 640, True, 0, torch.bfloat16, seed=3)
+    assert torch.equal(got[0], rec[0])
+
+
+def test_ws_too_small_rejected():
+    B, Hq, Hkv, N, D = 1, 2, 1, 256, 512
+    q, k, v, do = (t.to(DEV) for t in make_inputs(B, Hq, Hkv, N, D, seed=1))
+    o, lse = _fwd(q, k, v, True, 0, 1 / math.sqrt(D), True)
+    size = bwd_workspace_size(B, Hq, Hkv, N, D, True, 0)
+    ws = torch.empty(size - 256, dtype=torch.uint8, device=DEV)
+    with pytest.raises(ValueError):
+        _bwd(q, k, v, o, lse, do, True, 0, 1 / math.sqrt(D), workspace=ws)
+
+
+def test_default_path_uses_workspace_and_limit_env(monkeypatch):
+    """Default full backward at head_dim 512 = materialised path; a zero limit
+    selects the recomputing kernels; both agree."""
+    B, Hq, Hkv, N, D = 1, 4, 2, 384, 512
+    q, k, v, do = (t.to(DEV) for t in make_inputs(B, Hq, Hkv, N, D, seed=5))
+    o, lse = _fwd(q, k, v, True, 0, 1 / math.sqrt(D), True)
+    a = _bwd(q, k, v, o, lse, do, True, 0, 1 / math.sqrt(D))
+    monkeypatch.setenv("GQAFA_BWD_WORKSPACE_LIMIT", "0")
+    r = _bwd(q, k, v, o, lse, do, True, 0, 1 / math.sqrt(D))
+    torch.cuda.synchronize()
+    assert torch.equal(a[0], r[0])
+    for x, y in zip(a[1:], r[1:]):
+        assert (x.float() - y.float()).abs().max().item() <= 2e-2
