@@ -69,7 +69,7 @@ def parse_args():
     ap.add_argument("--strong", action="store_true",
                     help="strong scaling: one config-2 problem (B=1) split over the GPUs by (batch, KV-group) units, "
                          "and by sequence blocks when there are more GPUs than units; outputs all-gathered")
-    ap.add_argument("--only", choices=["fwd", "dq", "dk", "dv"], default=None,
+    ap.add_argument("--only", choices=["fwd", "dq", "dk", "dv", "dqps", "dkv"], default=None,
                     help="profiling mode: run only this kernel, warmup + steps launches, print nothing")
     return ap.parse_args()
 
@@ -240,8 +240,12 @@ def time_loop(fn, steps, stream):
 
 def run_ours(args, wl, world, rank, local):
     from gemma_triton_flash_attn import FlashAttnGQAFunction, _lib
-    from gemma_triton_flash_attn.attention import _bwd, _fwd
+    from gemma_triton_flash_attn.attention import _alloc_workspace, _bwd, _fwd, bwd_workspace_size
     from gemma_triton_flash_attn.flops import attn_flops, kernel_flops
+
+    def _bwd_workspace(*shape_args):
+        # the same workspace decision the public API's backward makes
+        return _alloc_workspace(bwd_workspace_size(*shape_args[:-1]), shape_args[-1])
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -255,15 +259,21 @@ def run_ours(args, wl, world, rank, local):
         o, lse = _fwd(q, k, v, causal, window, scale, True)
         bufs = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
                 torch.empty((B, Hq, N), dtype=torch.float32, device=device))
-        if args.only != "fwd":
+        ws = None
+        if args.only in ("dqps", "dkv"):
+            ws = _bwd_workspace(B, Hq, Hkv, N, D, causal, window, device)
+            if ws is None:
+                raise SystemExit("--only %s: no materialised backward for this workload" % args.only)
+            _bwd(q, k, v, o, lse, do, causal, window, scale, stage=0, out=bufs, workspace=ws)
+        elif args.only != "fwd":
             _bwd(q, k, v, o, lse, do, causal, window, scale, stage=0, out=bufs)  # delta for dK
         torch.cuda.synchronize()
-        stage = {"dq": 0, "dk": 1, "dv": 2}.get(args.only)
+        stage = {"dq": 0, "dk": 1, "dv": 2, "dqps": 0, "dkv": 1}.get(args.only)
         for _ in range(args.warmup + args.steps):
             if stage is None:
                 _fwd(q, k, v, causal, window, scale, True)
             else:
-                _bwd(q, k, v, o, lse, do, causal, window, scale, stage=stage, out=bufs)
+                _bwd(q, k, v, o, lse, do, causal, window, scale, stage=stage, out=bufs, workspace=ws)
         torch.cuda.synchronize()
         if _lib.device_status(local) != 0:
             raise RuntimeError("kernel status word set")
@@ -299,16 +309,26 @@ def run_ours(args, wl, world, rank, local):
     ms_fwd = max_over_ranks(time_loop(lambda: _fwd(q, k, v, causal, window, scale, True), args.steps, stream),
                             world, device)
 
-    # per-kernel timing for the roofline
+    ws_bytes = bwd_workspace_size(B, Hq, Hkv, N, D, causal, window)
+    # per-kernel timing for the roofline: the kernels the step above ran
     o, lse = _fwd(q, k, v, causal, window, scale, True)
     bufs = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
             torch.empty((B, Hq, N), dtype=torch.float32, device=device))
     kernels = {"fwd": ms_fwd}
-    for stage, name in enumerate(("dq", "dk", "dv")):
-        fn = lambda st=stage: _bwd(q, k, v, o, lse, do, causal, window, scale, stage=st, out=bufs)  # noqa: E731
+    ws = _bwd_workspace(B, Hq, Hkv, N, D, causal, window, device)
+    if ws is not None:  # materialised backward: dQ (+ P, dS stores), then dK + dV
+        names = ("dqps", "dkv")
+        mk = lambda st: (lambda: _bwd(q, k, v, o, lse, do, causal, window, scale, stage=st, out=bufs,  # noqa: E731
+                                      workspace=ws))
+    else:
+        names = ("dq", "dk", "dv")
+        mk = lambda st: (lambda: _bwd(q, k, v, o, lse, do, causal, window, scale, stage=st, out=bufs))  # noqa: E731
+    for stage, name in enumerate(names):
+        fn = mk(stage)
         fn()
         torch.cuda.synchronize()
         kernels[name] = time_loop(fn, args.steps, stream)
+    del ws
     status = _lib.device_status(local)
     dom = max(kernels, key=kernels.get)
     peaks = measured_peaks()
@@ -326,34 +346,58 @@ def run_ours(args, wl, world, rank, local):
                     kernel_ms={k_: round(v_, 3) for k_, v_ in kernels.items()},
                     kernel_share={k_: round(v_ / sum(kernels.values()), 3) for k_, v_ in kernels.items()})
 
-    # end to end through the public API with host buffers
+    # end to end through the public API with host buffers. Every step uploads
+    # its own q, k, v, dO from pinned host memory and downloads dQ, dK, dV;
+    # the copies run on their own streams, step s+1's upload (into the other
+    # of two input buffer sets) overlapping step s's kernels and step s's
+    # download overlapping step s+1's, as a prefetching input pipeline would.
     e2e = None
     if not args.no_e2e:
-        hq_, hk_, hv_, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
-        gq_h, gk_h, gv_h = (torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, k, v))
-        dq_, dk_, dv_ = (torch.empty_like(t) for t in (q, k, v))
+        host_in = [t.cpu().pin_memory() for t in (q, k, v, do)]
+        host_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, k, v)]
+        dev_in = [[torch.empty_like(t) for t in (q, k, v, do)] for _ in range(2)]
+        up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_free = [torch.cuda.Event() for _ in range(2)]
 
-        def e2e_step():
-            with torch.no_grad():
-                dq_.copy_(hq_, non_blocking=True)
-                dk_.copy_(hk_, non_blocking=True)
-                dv_.copy_(hv_, non_blocking=True)
-                do.copy_(hdo, non_blocking=True)
-            qq, kk, vv = (t.detach().requires_grad_(True) for t in (dq_, dk_, dv_))
-            out = FlashAttnGQAFunction.apply(qq, kk, vv, causal, W)
-            out.backward(do)
-            gq_h.copy_(qq.grad, non_blocking=True)
-            gk_h.copy_(kk.grad, non_blocking=True)
-            gv_h.copy_(vv.grad, non_blocking=True)
+        def upload(s):
+            buf = dev_in[s % 2]
+            with torch.cuda.stream(up):
+                if s >= 2:
+                    up.wait_event(ev_free[s % 2])
+                for d_, h_ in zip(buf, host_in):
+                    d_.copy_(h_, non_blocking=True)
+                ev_in[s % 2].record(up)
 
-        e2e_step()
+        def e2e_run(nsteps):
+            up.wait_stream(stream)  # uploads start inside the timed region
+            upload(0)
+            for s_ in range(nsteps):
+                if s_ + 1 < nsteps:
+                    upload(s_ + 1)
+                stream.wait_event(ev_in[s_ % 2])
+                xq, xk, xv, xdo = dev_in[s_ % 2]
+                qq, kk, vv = (t.detach().requires_grad_(True) for t in (xq, xk, xv))
+                out = FlashAttnGQAFunction.apply(qq, kk, vv, causal, W)
+                out.backward(xdo)
+                ev_free[s_ % 2].record(stream)
+                grads = (qq.grad, kk.grad, vv.grad)
+                down.wait_stream(stream)
+                with torch.cuda.stream(down):
+                    for h_, g_ in zip(host_out, grads):
+                        g_.record_stream(down)
+                        h_.copy_(g_, non_blocking=True)
+            stream.wait_stream(down)
+
+        e2e_run(2)
         torch.cuda.synchronize()
         barrier(world)
-        ms_e2e = max_over_ranks(time_loop(e2e_step, args.steps, stream), world, device)
-        h2d = sum(t.numel() * t.element_size() for t in (hq_, hk_, hv_, hdo))
-        d2h = sum(t.numel() * t.element_size() for t in (gq_h, gk_h, gv_h))
+        ms_e2e = max_over_ranks(time_loop(lambda: e2e_run(args.steps), 1, stream) / args.steps, world, device)
+        h2d = sum(t.numel() * t.element_size() for t in host_in)
+        d2h = sum(t.numel() * t.element_size() for t in host_out)
         e2e = dict(value=round(world * flops_step / (ms_e2e * 1e-3) / 1e12, 2), unit="TFLOPS/s",
-                   ms_per_step=round(ms_e2e, 3), h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h)
+                   ms_per_step=round(ms_e2e, 3), h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
+                   pipeline="copy streams; step s+1 upload and step s download overlap kernels")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -372,7 +416,8 @@ def run_ours(args, wl, world, rank, local):
             fwd=dict(value=round(world * flops_fwd / (ms_fwd * 1e-3) / 1e12, 2), unit="TFLOPS/s",
                      ms=round(ms_fwd, 3)),
             roofline=roofline, cpu_baseline=cpu, e2e=e2e, clocks=clocks.summary(),
-            gpu_launches=4 * args.steps, kernel_status=status,
+            gpu_launches=(1 + len(names)) * args.steps, kernel_status=status,
+            bwd_path="materialised (workspace %d bytes)" % ws_bytes if len(names) == 2 else "recompute",
         )
         print(json.dumps(line), flush=True)
 

@@ -25,8 +25,10 @@ def attn_flops(b: int, hq: int, n: int, d: int, causal: bool, window: int = 0, b
 
 # GEMMs (each 2*D*P FLOPs per query head) that each kernel's own math needs:
 # fwd Q.K^T and P.V; dQ recomputes Q.K^T, forms dO.V^T and dS.K; dK the same
-# two scores plus dS^T.Q; dV recomputes Q.K^T and forms P^T.dO.
-KERNEL_GEMMS = {"fwd": 2, "dq": 3, "dk": 3, "dv": 2}
+# two scores plus dS^T.Q; dV recomputes Q.K^T and forms P^T.dO. The
+# materialised backward's dQ kernel ("dqps") does the dQ kernel's three and
+# stores P and dS; its dK/dV kernel ("dkv") forms dS^T.Q and P^T.dO only.
+KERNEL_GEMMS = {"fwd": 2, "dq": 3, "dk": 3, "dv": 2, "dqps": 3, "dkv": 2}
 
 
 def kernel_flops(kernel: str, b: int, hq: int, n: int, d: int, causal: bool, window: int = 0) -> int:
