@@ -53,7 +53,11 @@ struct PairCfg {
   static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;
   static constexpr int PBUF_ONE = M * BN * 2;
   static constexpr int PBUF_BYTES = NS * PBUF_ONE;
-  static constexpr int NBARS = 2 * NSTAGES + 1 + 3 * NS + 2;
+  // dQ / dK with one S / dP buffer: the next item's S MMAs are issued as soon
+  // as the row warps have read S ("S free"), ahead of this item's accumulate
+  // MMAs, so the tensor pipe works while the row warps form dS.
+  static constexpr bool EARLY_S = HAS_DP && NS == 1;
+  static constexpr int NBARS = 2 * NSTAGES + 1 + 4 * NS + 2;
   // sRow (M floats), then for the forward the row-statistics exchange:
   // [2 slots][2 halves][M] maxima and [2 halves][M] partial sums.
   static constexpr int XCH_FLOATS = (ROLE == ROLE_FWD) ? 6 * M : 0;
@@ -104,6 +108,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   // S of the item is in TMEM (dP may still be in flight): lets the row warps
   // compute P while the dP MMAs run (dQ / dK).
   auto BAR_SREADY = [&](int s) { return bar0 + 8u * (2 * NST + 3 + 2 * NS + s); };
+  // The row warps of both CTAs have read S of the buffer (EARLY_S).
+  auto BAR_SFREE = [&](int s) { return bar0 + 8u * (2 * NST + 3 + 3 * NS + s); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -155,6 +161,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     for (int s = 0; s < NS; ++s) {
       mbar_init(BAR_SFULL(s), 1);
       mbar_init(BAR_SREADY(s), 1);
+      mbar_init(BAR_SFREE(s), 8);
       mbar_init(BAR_PREADY(s), 8);  // 4 row warps in each CTA of the pair
     }
     mbar_init(BAR_ACC, 1);
@@ -239,10 +246,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             }
         return true;
       };
-      for (int s = 0; s < NS && s < n_items && ok; ++s) ok = load_scores(s);
-      for (int i = 0; i < n_items && ok; ++i) {
-        ok = load_y(i);
-        if (ok && i + NS < n_items) ok = load_scores(i + NS);
+      if constexpr (C::EARLY_S) {
+        // the issuer's order: S(0) dP(0), then per item S(i+1), acc(i), dP(i+1)
+        auto load_s = [&](int i) { return load_c(&tmC1, item_col0(i), item_headC(i)); };
+        auto load_dp = [&](int i) { return load_c(&tmC2, item_col0(i), item_headC(i)); };
+        if (n_items > 0) ok = load_s(0) && load_dp(0);
+        for (int i = 0; i < n_items && ok; ++i) {
+          if (i + 1 < n_items) ok = load_s(i + 1);
+          ok = ok && load_y(i);
+          if (ok && i + 1 < n_items) ok = load_dp(i + 1);
+        }
+      } else {
+        for (int s = 0; s < NS && s < n_items && ok; ++s) ok = load_scores(s);
+        for (int i = 0; i < n_items && ok; ++i) {
+          ok = load_y(i);
+          if (ok && i + NS < n_items) ok = load_scores(i + NS);
+        }
       }
     }
   } else if (warp == 1) {
@@ -334,10 +353,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         cnt += C::Y_STAGES;
         return true;
       };
-      for (int s = 0; s < NS && s < n_items && ok; ++s) ok = issue_scores(s);
-      for (int i = 0; i < n_items && ok; ++i) {
-        ok = issue_acc(i);
-        if (ok && i + NS < n_items) ok = issue_scores(i + NS);
+      if constexpr (C::EARLY_S) {
+        auto issue_s = [&](int i) -> bool {
+          if (!scores_from(dR1, tbase + C::ACC_COLS)) return false;
+          mma_commit_pair(BAR_SREADY(0));
+          return true;
+        };
+        auto issue_dp = [&](int i) -> bool {
+          if (!scores_from(dR2, tbase + C::ACC_COLS + C::SBUF_COLS)) return false;
+          mma_commit_pair(BAR_SFULL(0));
+          return true;
+        };
+        if (n_items > 0) ok = issue_s(0) && issue_dp(0);
+        for (int i = 0; i < n_items && ok; ++i) {
+          if (i + 1 < n_items) {
+            const long long t0 = tick();
+            ok = mbar_wait_cluster(BAR_SFREE(0), i & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY);
+            tock(WC_MMA_PREADY, t0);
+            if (ok) {
+              tc_fence_after();
+              ok = issue_s(i + 1);
+            }
+          }
+          // dP(i+1) overwrites dP(i), which the row warps have read once they
+          // signal P ready for item i (issue_acc waits for that).
+          ok = ok && issue_acc(i);
+          if (ok && i + 1 < n_items) ok = issue_dp(i + 1);
+        }
+      } else {
+        for (int s = 0; s < NS && s < n_items && ok; ++s) ok = issue_scores(s);
+        for (int i = 0; i < n_items && ok; ++i) {
+          ok = issue_acc(i);
+          if (ok && i + NS < n_items) ok = issue_scores(i + NS);
+        }
       }
       if (ok) mma_commit_pair(BAR_FINAL);
     }
@@ -355,6 +403,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     float row_lse2 = 0.f, row_delta = 0.f;
     const long long rowbase_q = (static_cast<long long>(b) * p.Hq + (C::ROWS_ARE_Q ? h : 0)) * N;
     const uint32_t pready_l0 = mapa_shared(BAR_PREADY(0), 0);
+    const uint32_t sfree_l0 = mapa_shared(BAR_SFREE(0), 0);
 
     if constexpr (C::ROLE == ROLE_DQ) {
       const uint16_t* Og = reinterpret_cast<const uint16_t*>(p.o) + b * p.o_sb + h * p.o_sh;
@@ -639,9 +688,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             }
           }
         }
+        if constexpr (C::EARLY_S) {
+          if (ok) {  // S is in registers: the issuer may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(sfree_l0);
+          }
+        }
         if (ws_on) {
-          // P -> buffer -> workspace. The previous item's dS store must have
-          // finished reading the buffer; its MMAs have (S-ready implies it).
+          // P -> buffer -> workspace. The buffer still holds dS of the previous
+          // item: wait for its accumulate MMAs (with EARLY_S, S-ready no longer
+          // implies them) and for its TMA store to have read it.
+          if (C::EARLY_S && i > 0 && ok) {
+            ok = mbar_wait_cluster(BAR_ACC, (i - 1) & 1u, abort_flag, p.status, ST_TIMEOUT_ACC);
+            ok = __all_sync(0xffffffffu, ok);
+          }
           if (tid0) bulk_wait_read0();
           row_bar();
           if (ok) {
