@@ -1,4 +1,4 @@
-// Head_dim-512 dK + dV from materialised P and dS (CTA pairs, cta_group::2).
+// dK + dV from materialised P and dS (CTA pairs, cta_group::2).
 //
 // Replaces the reference's packed dK/dV launch (flash_attn/attention.py:
 // 1602-1620) when the dQ kernel has written P and dS to a workspace (see
@@ -9,7 +9,7 @@
 //   dV[k rows] += P^T dO      dK[k rows] += dS^T Q      (dK scaled at the end)
 //
 // A pair owns 128 key rows (64 per CTA). Both fp32 accumulators stay in TMEM
-// for the whole kernel: dK in columns 0-255, dV in 256-511 of each CTA, in
+// for the whole kernel: dK in columns [0, D/2), dV in [D/2, D) of each CTA, in
 // the 2x2 layout of attn_pair_kernel.cuh. P^T and dS^T are read as MN-major A
 // operands straight from the workspace's [128 queries][256 keys] blocks (a TMA
 // box of 64 keys x 128 queries per CTA); Q and dO are MN-major B operands
@@ -35,6 +35,7 @@ struct DkvCfg {
   static constexpr int M = 64, MP = 128;
   static constexpr int BN = 256;            // query rows per item (two 128-row query tiles)
   static constexpr int NACC = D / 256;      // N=256 pair instructions per accumulator and k-step
+  static constexpr int ACC_COLS = D / 2;    // TMEM columns of one accumulator per CTA
   static constexpr int STAGE_BYTES = 128 * 128;
   static constexpr int SUB_STAGES = 2 + 4 * NACC;
   static constexpr int Y_BOX = 128;
@@ -42,7 +43,7 @@ struct DkvCfg {
   static constexpr int SMEM_BYTES = 1024 + NSTAGES * STAGE_BYTES + NBARS * 8 + 16;
   static constexpr uint32_t IDESC = make_idesc(MP, 256, BF16, true, true);
 
-  static_assert(D == 512, "the dK/dV accumulators fill TMEM exactly at head_dim 512");
+  static_assert(D % 256 == 0 && 2 * ACC_COLS <= 512, "dK and dV accumulators in TMEM");
   static_assert(NSTAGES % 2 == 0 && NSTAGES >= SUB_STAGES, "ring");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
@@ -193,7 +194,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
               tc_fence_after();
               const uint64_t a = (m == 0) ? aDS : aP;
               const uint64_t yb = sdesc(c2);
-              const uint32_t acc = (m == 0 ? 0u : 256u) + 128u * g;
+              const uint32_t acc = m * C::ACC_COLS + 128u * g;
 #pragma unroll
               for (int tt = 0; tt < 8; ++tt) {
                 const uint64_t off = static_cast<uint64_t>((tt * 2048) >> 4);
@@ -245,7 +246,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             float v[32];
             if (any) {
               uint32_t r[32];
-              tmem_ld32(tq + 256 * m + g * 128 + 32 * k, r);
+              tmem_ld32(tq + C::ACC_COLS * m + g * 128 + 32 * k, r);
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * mul;
             } else {

@@ -191,7 +191,13 @@ template <bool BF16> using Dq512 = PairCfg<ROLE_DQ, 512, 256, 1, 4, BF16>;
 template <bool BF16> using Dk512 = PairCfg<ROLE_DK, 512, 256, 1, 4, BF16>;
 template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 256, 2, 6, BF16>;
 
+// Materialised backward (gqafa_bwd_ws): a pair dQ kernel that also stores P
+// and dS, then the dK + dV kernel. At head_dim 256 the dQ kernel is the
+// pair configuration with 256-key items (the recomputing path keeps the
+// 1-CTA Dq256).
 template <bool BF16> using Dkv512 = DkvCfg<512, 14, BF16>;
+template <bool BF16> using DqWs256 = PairCfg<ROLE_DQ, 256, 256, 1, 8, BF16>;
+template <bool BF16> using Dkv256 = DkvCfg<256, 14, BF16>;
 
 struct Problem {
   int B, Hq, Hkv, N, D, causal, window;
@@ -365,19 +371,17 @@ long long ws_blocks_per_head(const Problem& pr) {
 }
 
 long long ws_bytes(const Problem& pr) {
-  if (pr.D != 512) return 0;
+  if (pr.D != 256 && pr.D != 512) return 0;
   return 2LL * pr.B * pr.Hq * ws_blocks_per_head(pr) * (128LL * 256 * 2);
 }
 
 // Materialised head_dim-512 backward: stage bit 1 = dQ + delta, writing P and
 // dS to the workspace; bit 2 = dK and dV from them.
-template <bool BF16>
+template <bool BF16, class CQ, class CKV>
 int bwd_ws_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const TensorDesc& v,
                 const TensorDesc& o, const TensorDesc& dout, const float* lse, void* dq, const TensorDesc& dqd,
                 void* dk, const TensorDesc& dkd, void* dv, const TensorDesc& dvd, float* delta, void* ws,
                 cudaStream_t st, int stages) {
-  using CQ = Dq512<BF16>;
-  using CKV = Dkv512<BF16>;
   int* status = status_ptr();
   if (!status) return fail(GQAFA_ERR_CUDA, "cannot resolve the device status word");
   const long long bph = ws_blocks_per_head(pr);
@@ -612,10 +616,15 @@ static int bwd_ws_entry(int stages, GQAFA_BWD_PARAMS, void* workspace, long long
   if (lse == nullptr || delta == nullptr) return fail(GQAFA_ERR_INVALID, "lse and delta must be non-null");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = bind_device(st))) return rc;
-  return pr.bf16 ? bwd_ws_impl<true>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk, dkd, dv, dvd, delta, workspace, st,
-                                     stages)
-                 : bwd_ws_impl<false>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk, dkd, dv, dvd, delta, workspace, st,
-                                      stages);
+  if (pr.D == 256)
+    return pr.bf16 ? bwd_ws_impl<true, DqWs256<true>, Dkv256<true>>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk, dkd, dv,
+                                                                     dvd, delta, workspace, st, stages)
+                   : bwd_ws_impl<false, DqWs256<false>, Dkv256<false>>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk, dkd,
+                                                                        dv, dvd, delta, workspace, st, stages);
+  return pr.bf16 ? bwd_ws_impl<true, Dq512<true>, Dkv512<true>>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk, dkd, dv,
+                                                                 dvd, delta, workspace, st, stages)
+                 : bwd_ws_impl<false, Dq512<false>, Dkv512<false>>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk, dkd, dv,
+                                                                    dvd, delta, workspace, st, stages);
 }
 
 extern "C" int gqafa_bwd_ws(GQAFA_BWD_PARAMS, void* workspace, long long workspace_bytes) {

@@ -232,7 +232,7 @@ def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=
     with `rows` = (begin, end) only those rows (query rows for stage 0, key rows
     for stages 1 and 2).
 
-    A full backward (no stage, no rows) at head_dim 512 takes the materialised
+    A full backward (no stage, no rows) takes the materialised
     path (gqafa_bwd_ws: the dQ kernel stores P and dS, one kernel makes dK and
     dV from them) with a workspace from the caching allocator, or `workspace`
     when given; without the memory it runs the recomputing gqafa_bwd. With a

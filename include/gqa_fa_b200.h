@@ -104,18 +104,19 @@ GQAFA_API int gqafa_bwd_noalloc(const void* q, const long long* q_strides, const
                                 int head_dim, float softmax_scale, int causal, int window, int dtype,
                                 void* stream);
 
-/* Materialised backward (head_dim 512). The reference's dK/dV launch
- * recomputes S = Q K^T and dP = dO V^T for every (key tile, query block)
+/* Materialised backward. The reference's dK/dV launch recomputes
+ * S = Q K^T and dP = dO V^T for every (key tile, query block)
  * (flash_attn/attention.py:1602-1620) after its dQ launch already computed
  * them (flash_attn/attention.py:1506-1523). gqafa_bwd_ws instead has the dQ
  * kernel also write P and dS (16-bit, the attended 128 x 256 blocks only) to a
  * caller-provided workspace and computes dK and dV from them in one kernel:
- * 10 instead of 16 head_dim-sized MACs per attended (query, key) pair.
- * Same arguments and results as gqafa_bwd, plus the workspace (256-byte
- * aligned device memory, any contents). gqafa_bwd_workspace_size returns the
- * bytes it needs (2 * B * H_Q * blocks * 64 KiB), 0 where the materialised
- * path does not apply (head_dim 256: gqafa_bwd_ws then runs gqafa_bwd and
- * ignores the workspace), or -1 for invalid sizes. */
+ * 10 instead of 16 head_dim-sized MACs per attended (query, key) pair, and
+ * the softmax elementwise work done once. Same arguments and results as
+ * gqafa_bwd, plus the workspace (256-byte aligned device memory, any
+ * contents). gqafa_bwd_workspace_size returns the bytes it needs
+ * (2 * B * H_Q * blocks * 64 KiB, independent of head_dim), 0 where the
+ * materialised path does not apply (gqafa_bwd_ws then runs gqafa_bwd and
+ * ignores the workspace), or -1 for invalid or unsupported sizes. */
 GQAFA_API long long gqafa_bwd_workspace_size(int batch, int heads_q, int heads_kv, int seqlen, int head_dim,
                                              int causal, int window);
 GQAFA_API int gqafa_bwd_ws(const void* q, const long long* q_strides, const void* k, const long long* k_strides,

@@ -108,5 +108,6 @@ def test_bwd_workspace_size(n, causal, window):
     w = window if (causal and 0 < window < n) else 0
     want = 2 * 2 * 8 * _blocks_per_head(n, causal, w) * 128 * 256 * 2
     assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 512, int(causal), window) == want
-    assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 256, int(causal), window) == 0
+    assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 256, int(causal), window) == want
+    assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 128, int(causal), window) == -1
     assert lib.gqafa_bwd_workspace_size(2, 8, 3, n, 512, int(causal), window) == -1
