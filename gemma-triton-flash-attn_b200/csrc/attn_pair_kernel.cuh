@@ -466,33 +466,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         tock(WC_ROW_SFULL, t_w);
         const long long t_work = tick();
         const uint32_t s_col = C::ACC_COLS + sb * C::SBUF_COLS;
-        float s[KCH][32];
+        // Two passes over S in TMEM, 32 columns at a time with rolled loops:
+        // the row max, then exp2 / sum / pack into the P buffer. Re-reading S
+        // costs TMEM bandwidth, which is plentiful; unrolling both passes over
+        // all columns would multiply the code size, and the instruction cache
+        // is shared with the MMA-issuing thread.
+        int lo_abs, hi_abs;
+        attended_interval(true, r0 + row, N, p.causal, p.window, lo_abs, hi_abs);
+        const int lo_rel = lo_abs - cb;
+        const unsigned span = span_of(lo_rel, hi_abs - cb);
         float mx = -INFINITY;
         if (ok) {
           tc_fence_after();
-          int lo_abs, hi_abs;
-          attended_interval(true, r0 + row, N, p.causal, p.window, lo_abs, hi_abs);
-          const int lo_rel = lo_abs - cb;
-          const unsigned span = span_of(lo_rel, hi_abs - cb);
-          constexpr int KB = KCH < 2 ? KCH : 2;
+#pragma unroll 1
+          for (int kb = 0; kb < KCH; kb += 2) {
+            uint32_t rs[2][32];
+            tmem_ld32_async(tq + s_col + 32 * kb, rs[0]);
+            tmem_ld32_async(tq + s_col + 32 * (kb + 1), rs[1]);
+            tmem_ld_wait32(rs[0]);
+            tmem_ld_wait32(rs[1]);
 #pragma unroll
-          for (int kb = 0; kb < KCH; kb += KB) {
-            uint32_t rs[KB][32];
-#pragma unroll
-            for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + s_col + 32 * (kb + u), rs[u]);
-#pragma unroll
-            for (int u = 0; u < KB; ++u) tmem_ld_wait32(rs[u]);
-#pragma unroll
-            for (int u = 0; u < KB; ++u) {
+            for (int u = 0; u < 2; ++u) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 const int c = 32 * (kb + u) + j;
-                const float x = __uint_as_float(rs[u][j]) * sl2;
-                s[kb + u][j] = (static_cast<unsigned>(c - lo_rel) < span) ? x : -INFINITY;
-                mx = fmaxf(mx, s[kb + u][j]);
+                const float x = __uint_as_float(rs[u][j]);
+                mx = (static_cast<unsigned>(c - lo_rel) < span) ? fmaxf(mx, x) : mx;
               }
             }
           }
+          mx *= sl2;  // sl2 > 0, so the max commutes with the scaling
         }
         float* xm = sX + (i & 1) * 2 * M;
         xm[half * M + row] = mx;
@@ -511,12 +514,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         }
         const float ms = (m_run == -INFINITY) ? 0.f : m_run;
         float sum = 0.f;
-#pragma unroll
+#pragma unroll 1
         for (int k = 0; k < KCH; ++k) {
+          uint32_t r[32];
+          tmem_ld32(tq + s_col + 32 * k, r);
+          float e[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            s[k][j] = ex2(s[k][j] - ms);
-            sum += s[k][j];
+            const int c = 32 * k + j;
+            const float x = ex2(__uint_as_float(r[j]) * sl2 - ms);
+            e[j] = (static_cast<unsigned>(c - lo_rel) < span) ? x : 0.f;
+            sum += e[j];
+          }
+          // K-major SWIZZLE_128B [64 rows x BN] tile of 64-column panels.
+          const int col = half * (BN / 2) + 32 * k;
+          uint8_t* prow = sP + sb * C::PBUF_ONE + (col / 64) * (M * 128) + row * 128;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int chunk16 = (col % 64) / 8 + cc;
+            uint4 w;
+            w.x = pack2<C::BF16>(e[8 * cc + 0], e[8 * cc + 1]);
+            w.y = pack2<C::BF16>(e[8 * cc + 2], e[8 * cc + 3]);
+            w.z = pack2<C::BF16>(e[8 * cc + 4], e[8 * cc + 5]);
+            w.w = pack2<C::BF16>(e[8 * cc + 6], e[8 * cc + 7]);
+            *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (row & 7)) * 16)) = w;
           }
         }
         l_run = l_run * alpha + sum;
@@ -542,22 +563,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             }
           }
           tmem_st_wait();
-        }
-#pragma unroll
-        for (int k = 0; k < KCH; ++k) {
-          // K-major SWIZZLE_128B [64 rows x BN] tile of 64-column panels.
-          const int col = half * (BN / 2) + 32 * k;
-          uint8_t* prow = sP + sb * C::PBUF_ONE + (col / 64) * (M * 128) + row * 128;
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            const int chunk16 = (col % 64) / 8 + cc;
-            uint4 w;
-            w.x = pack2<C::BF16>(s[k][8 * cc + 0], s[k][8 * cc + 1]);
-            w.y = pack2<C::BF16>(s[k][8 * cc + 2], s[k][8 * cc + 3]);
-            w.z = pack2<C::BF16>(s[k][8 * cc + 4], s[k][8 * cc + 5]);
-            w.w = pack2<C::BF16>(s[k][8 * cc + 6], s[k][8 * cc + 7]);
-            *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (row & 7)) * 16)) = w;
-          }
         }
         tc_fence_before();
         fence_proxy_async_smem();
