@@ -85,18 +85,58 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks + throttle reasons sampled every 200 ms while running."""
+    """SM clocks and throttle reasons sampled while the timed steps run.
+
+    NVML (read-only queries) from a background thread every 20 ms, so even a
+    timed region of a few hundred ms gets samples; the first sample is taken
+    before __enter__ returns. Falls back to `nvidia-smi -lms 200` without NVML."""
 
     FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h)
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, uuids):
-        self.uuids = set(uuids)
+    def __init__(self, uuids, period_s=0.02):
+        self.uuids = list(uuids)
+        self.period = period_s
         self.proc = None
+        self.thread = None
+        self.samples = []  # (sm_mhz, max_mhz, reason bits)
         self.path = os.path.join("/tmp", f"gqafa_clocks_{os.getpid()}.csv")
 
+    def _nvml_start(self):
+        import threading
+
+        import pynvml
+        pynvml.nvmlInit()
+        handles = [pynvml.nvmlDeviceGetHandleByUUID(u) for u in self.uuids]
+        get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+        def sample():
+            for h in handles:
+                self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                     pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                     int(get_reasons(h))))
+
+        self.stop = threading.Event()
+
+        def loop():
+            while not self.stop.wait(self.period):
+                sample()
+
+        sample()
+        self.thread = threading.Thread(target=loop, daemon=True)
+        self.thread.start()
+
     def __enter__(self):
+        try:
+            self._nvml_start()
+            return self
+        except Exception:  # no NVML: nvidia-smi
+            self.thread = None
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -106,6 +146,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -116,6 +159,16 @@ class ClockSampler:
         return False
 
     def summary(self):
+        if self.thread is not None:
+            if not self.samples:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+            bits = 0
+            for _, _, r in self.samples:
+                bits |= r
+            reasons = sorted(n for n, b in self.REASON_BITS.items() if bits & b)
+            return {"sm_mhz": statistics.median(x[0] for x in self.samples),
+                    "sm_max_mhz": max(x[1] for x in self.samples), "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml, 20 ms"}
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         mhz, maxes, reasons = [], [], set()
@@ -137,7 +190,7 @@ class ClockSampler:
         if not mhz:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
-                "samples": len(mhz)}
+                "samples": len(mhz), "source": "nvidia-smi, 200 ms"}
 
 
 def setup_dist():
