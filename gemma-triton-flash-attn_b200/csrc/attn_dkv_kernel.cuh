@@ -15,11 +15,13 @@
 // box of 64 keys x 128 queries per CTA); Q and dO are MN-major B operands
 // split along head_dim between the two CTAs, as in the other pair kernels.
 //
-// Per query tile ("sub-item") the ring carries 10 stages of 16 KB in this
-// order: dS^T, P^T, then for g = 0, 1 the two 64-column panels of Q and the
-// two of dO for head_dim columns 256g + 128 * rank + [0, 128). The A stages
-// are held for the whole sub-item, the B stages are released in pairs, so
-// the ring needs at least 10 stages. Every wait is bounded as elsewhere.
+// Ring stages are 32 KB = two 16 KB panels under one barrier (half the
+// barrier waits and commits of 16 KB stages for the single issuing thread).
+// Per query tile ("sub-item") the ring carries 1 + 2 * D/256 stages in this
+// order: [dS^T | P^T], then for g = 0 .. D/256-1 the two 64-column panels of
+// Q and then of dO for head_dim columns 256g + 128 * rank + [0, 128). The A
+// stage is held for the whole sub-item, the B stages are released as they
+// are consumed. Every wait is bounded as elsewhere.
 #pragma once
 #include "attn_kernel.cuh"
 
@@ -36,15 +38,16 @@ struct DkvCfg {
   static constexpr int BN = 256;            // query rows per item (two 128-row query tiles)
   static constexpr int NACC = D / 256;      // N=256 pair instructions per accumulator and k-step
   static constexpr int ACC_COLS = D / 2;    // TMEM columns of one accumulator per CTA
-  static constexpr int STAGE_BYTES = 128 * 128;
-  static constexpr int SUB_STAGES = 2 + 4 * NACC;
+  static constexpr int PANEL_BYTES = 128 * 128;      // 128 rows x 64 columns, 16-bit
+  static constexpr int STAGE_BYTES = 2 * PANEL_BYTES;
+  static constexpr int SUB_STAGES = 1 + 2 * NACC;
   static constexpr int Y_BOX = 128;
   static constexpr int NBARS = 2 * NSTAGES + 1;
   static constexpr int SMEM_BYTES = 1024 + NSTAGES * STAGE_BYTES + NBARS * 8 + 16;
   static constexpr uint32_t IDESC = make_idesc(MP, 256, BF16, true, true);
 
   static_assert(D % 256 == 0 && 2 * ACC_COLS <= 512, "dK and dV accumulators in TMEM");
-  static_assert(NSTAGES % 2 == 0 && NSTAGES >= SUB_STAGES, "ring");
+  static_assert(NSTAGES >= SUB_STAGES, "ring");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
@@ -142,24 +145,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           before += jn;
           if (!(kblk >= jlo && kblk < jlo + jn)) continue;
           int st;
-          // dS^T then P^T: 128 queries x this CTA's 64 keys of the block
+          // [dS^T | P^T]: 128 queries x this CTA's 64 keys of the block, each
           ok = acquire(st);
           if (!ok) break;
-          tma_load_3d_pair(smem_u32(sRing + st * C::STAGE_BYTES), &tmWS, mapa_shared(BAR_FULL(st), 0), kcol, 0,
+          const uint32_t full_l = mapa_shared(BAR_FULL(st), 0);
+          tma_load_3d_pair(smem_u32(sRing + st * C::STAGE_BYTES), &tmWS, full_l, kcol, 0,
                            static_cast<int>(p.ws_blocks + blk));
-          ok = acquire(st);
-          if (!ok) break;
-          tma_load_3d_pair(smem_u32(sRing + st * C::STAGE_BYTES), &tmWS, mapa_shared(BAR_FULL(st), 0), kcol, 0,
+          tma_load_3d_pair(smem_u32(sRing + st * C::STAGE_BYTES + C::PANEL_BYTES), &tmWS, full_l, kcol, 0,
                            static_cast<int>(blk));
           for (int g = 0; g < C::NACC && ok; ++g) {
             for (int m = 0; m < 2 && ok; ++m) {
               const CUtensorMap* map = (m == 0) ? &tmQ : &tmDO;
-              for (int j = 0; j < 2; ++j) {
-                ok = acquire(st);
-                if (!ok) break;
-                tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES), map, mapa_shared(BAR_FULL(st), 0),
+              ok = acquire(st);
+              if (!ok) break;
+              const uint32_t fl = mapa_shared(BAR_FULL(st), 0);
+              for (int j = 0; j < 2; ++j)
+                tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES + j * C::PANEL_BYTES), map, fl,
                                  64 * (4 * g + 2 * static_cast<int>(rank) + j), 128 * t, hq, b);
-              }
             }
           }
         }
@@ -171,7 +173,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       bool ok = true;
       uint32_t cnt = 0;
       bool first = true;
-      const uint64_t dRing = sw128_desc(smem_u32(sRing), C::STAGE_BYTES, 1024);
+      const uint64_t dRing = sw128_desc(smem_u32(sRing), C::PANEL_BYTES, 1024);
       auto full = [&](uint32_t c) {
         return mbar_wait_cluster(BAR_FULL(c % NST), (c / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL);
       };
@@ -179,17 +181,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       for (int g0 = 0; g0 < G && ok; ++g0) {
         for (int t = t_lo; t < t_hi && ok; ++t) {
           if (!stored(t)) continue;
-          const uint32_t cA = cnt;  // dS^T at cA, P^T at cA + 1
-          ok = full(cA) && full(cA + 1);
+          const uint32_t cA = cnt;  // [dS^T | P^T]
+          ok = full(cA);
           if (!ok) break;
           tc_fence_after();
-          const uint64_t aDS = sdesc(cA), aP = sdesc(cA + 1);
+          const uint64_t aDS = sdesc(cA), aP = aDS + static_cast<uint64_t>(C::PANEL_BYTES >> 4);
 #pragma unroll 1
           for (int g = 0; g < C::NACC && ok; ++g) {
 #pragma unroll 1
             for (int m = 0; m < 2; ++m) {
-              const uint32_t c2 = cA + 2 + 4 * g + 2 * m;
-              ok = full(c2) && full(c2 + 1);
+              const uint32_t c2 = cA + 1 + 2 * g + m;
+              ok = full(c2);
               if (!ok) break;
               tc_fence_after();
               const uint64_t a = (m == 0) ? aDS : aP;
@@ -201,13 +203,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                 mma_ss_pair(tbase + acc, a + off, yb + off, C::IDESC, (first && tt == 0) ? 0u : 1u);
               }
               mma_commit_pair(BAR_EMPTY(c2 % NST));
-              mma_commit_pair(BAR_EMPTY((c2 + 1) % NST));
             }
           }
           if (!ok) break;
           first = false;
           mma_commit_pair(BAR_EMPTY(cA % NST));
-          mma_commit_pair(BAR_EMPTY((cA + 1) % NST));
           cnt += C::SUB_STAGES;
         }
       }

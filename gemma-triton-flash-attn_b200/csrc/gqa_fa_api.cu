@@ -195,9 +195,9 @@ template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 256, 2, 6, BF16>;
 // and dS, then the dK + dV kernel. At head_dim 256 the dQ kernel is the
 // pair configuration with 256-key items (the recomputing path keeps the
 // 1-CTA Dq256).
-template <bool BF16> using Dkv512 = DkvCfg<512, 14, BF16>;
+template <bool BF16> using Dkv512 = DkvCfg<512, 7, BF16>;
 template <bool BF16> using DqWs256 = PairCfg<ROLE_DQ, 256, 256, 1, 8, BF16>;
-template <bool BF16> using Dkv256 = DkvCfg<256, 14, BF16>;
+template <bool BF16> using Dkv256 = DkvCfg<256, 7, BF16>;
 
 struct Problem {
   int B, Hq, Hkv, N, D, causal, window;
