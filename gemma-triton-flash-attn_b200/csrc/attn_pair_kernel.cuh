@@ -40,16 +40,21 @@ struct PairCfg {
   static constexpr int PANELS_D = D / 64;
   static constexpr int R_PANEL = M * 128;
   static constexpr int R_BYTES = PANELS_D * R_PANEL * (HAS_DP ? 2 : 1);
-  // Ring stages are 16 KB: 128 rows of one 64-column panel.
-  static constexpr int STAGE_BYTES = 128 * 128;
+  // Ring stages are 32 KB, one barrier each: two 16 KB panels of 128 rows x
+  // 64 columns (fewer barrier waits and commits for the single issuing
+  // thread than one panel per stage).
+  static constexpr int PANEL_BYTES = 128 * 128;
+  static constexpr int STAGE_BYTES = 2 * PANEL_BYTES;
   static constexpr int CR = BN / 2;                     // score-operand rows this CTA loads per item
-  static constexpr int CP = 128 / CR;                   // score-operand panels per stage (2 or 1)
   static constexpr int C_PANEL_BYTES = CR * 128;
+  static constexpr int CP = STAGE_BYTES / C_PANEL_BYTES;  // score-operand panels per stage (2 or 4)
   static constexpr int C_STAGES = PANELS_D / CP;
   static constexpr int C_BOX = CR, Y_BOX = 128;
   static constexpr int NACC = D / 256;                  // N=256 accumulate instructions per k-step
-  static constexpr int YH = BN / 128;                   // 128-row stages per accumulate panel
-  static constexpr int Y_STAGES = NACC * 2 * YH;        // this CTA's 128 of every 256 columns
+  static constexpr int YH = BN / 128;                   // 128-row halves of an accumulate operand
+  // one stage per (instruction g, half hh): this CTA's two 64-column panels of
+  // its 128 of every 256 columns
+  static constexpr int Y_STAGES = NACC * YH;
   static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;
   static constexpr int PBUF_ONE = M * BN * 2;
   static constexpr int PBUF_BYTES = NS * PBUF_ONE;
@@ -71,7 +76,7 @@ struct PairCfg {
   static_assert(D % 256 == 0, "D");
   static_assert(BN == 128 || BN == 256, "BN");
   static_assert(ACC_COLS + NS * SBUF_COLS * (HAS_DP ? 2 : 1) <= 512, "TMEM");
-  static_assert(NSTAGES % 2 == 0, "ring groups");
+  static_assert(PANELS_D % CP == 0, "score-operand stages");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
@@ -234,16 +239,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       };
       auto load_y = [&](int i) -> bool {
         const int c0 = item_col0(i), hc = item_headC(i);
-        // stage order: [instruction g][128-row half hh][panel j]; the two panels of
-        // one (g, hh) are adjacent, which is the MN-major operand's LBO.
+        // stage order: [instruction g][128-row half hh]; a stage holds panels
+        // j = 0, 1 PANEL_BYTES apart, which is the MN-major operand's LBO.
         for (int g = 0; g < C::NACC; ++g)
-          for (int hh = 0; hh < C::YH; ++hh)
-            for (int j = 0; j < 2; ++j) {
-              int st;
-              if (!acquire(st)) return false;
-              tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES), &tmY, mapa_shared(BAR_FULL(st), 0),
+          for (int hh = 0; hh < C::YH; ++hh) {
+            int st;
+            if (!acquire(st)) return false;
+            const uint32_t fl = mapa_shared(BAR_FULL(st), 0);
+            for (int j = 0; j < 2; ++j)
+              tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES + j * C::PANEL_BYTES), &tmY, fl,
                                64 * (4 * g + 2 * static_cast<int>(rank) + j), c0 + 128 * hh, hc, b);
-            }
+          }
         return true;
       };
       if constexpr (C::EARLY_S) {
@@ -277,7 +283,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       // pair MMA with N=128 occupies the tensor pipe for only ~32 cycles.
       const uint64_t dR1 = sw128_desc(aR1, 16, 1024), dR2 = sw128_desc(aR2, 16, 1024);
       const uint64_t dRingK = sw128_desc(aRing, 16, 1024);
-      const uint64_t dRingMN = sw128_desc(aRing, C::STAGE_BYTES, 1024);
+      const uint64_t dRingMN = sw128_desc(aRing, C::PANEL_BYTES, 1024);
       const uint64_t dP = sw128_desc(aP, 16, 1024);
       auto scores_from = [&](uint64_t dR, uint32_t d_tmem) -> bool {
 #pragma unroll
@@ -319,22 +325,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         if (!mbar_wait_cluster(BAR_PREADY(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY))
           return false;
         tock(WC_MMA_PREADY, t0);
-        // Accumulate operand stages are consumed two at a time (the two panels of
-        // one instruction g and 128-row half hh) and released right after their
-        // MMAs, so an item never needs more ring stages at once than the ring has.
+        // Accumulate operand stages (both panels of one instruction g and
+        // 128-row half hh) are released right after their MMAs, so an item never
+        // needs more ring stages at once than the ring has.
         const uint64_t pb = dP + static_cast<uint64_t>((sb * C::PBUF_ONE) >> 4);
         const uint32_t acc0 = (i > 0) ? 1u : 0u;
 #pragma unroll
         for (int g = 0; g < C::NACC; ++g) {
 #pragma unroll
           for (int hh = 0; hh < C::YH; ++hh) {
-            const uint32_t c2 = cnt + 2 * (g * C::YH + hh);
+            const uint32_t c2 = cnt + g * C::YH + hh;
             t0 = tick();
-            for (int j = 0; j < 2; ++j) {
-              if (!mbar_wait_cluster(BAR_FULL((c2 + j) % NST), ((c2 + j) / NST) & 1u, abort_flag, p.status,
-                                     ST_TIMEOUT_RING_FULL))
-                return false;
-            }
+            if (!mbar_wait_cluster(BAR_FULL(c2 % NST), (c2 / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL))
+              return false;
             tock(WC_MMA_FULL_Y, t0);
             tc_fence_after();
             const uint64_t yb = dRingMN + static_cast<uint64_t>(((c2 % NST) * C::STAGE_BYTES) >> 4);
@@ -346,7 +349,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                           t > 0 ? 1u : acc0);
             }
             mma_commit_pair(BAR_EMPTY(c2 % NST));
-            mma_commit_pair(BAR_EMPTY((c2 + 1) % NST));
           }
         }
         mma_commit_pair(BAR_ACC);

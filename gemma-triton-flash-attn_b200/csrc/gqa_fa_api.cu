@@ -180,23 +180,23 @@ int launch(const CUtensorMap (&maps)[6], KParams p, cudaStream_t stream) {
 // Fixed configurations. Cfg<ROLE, M, D, DC, BN, NS, NSTAGES, YGROUP, BF16>
 template <bool BF16> using Fwd256 = Cfg<ROLE_FWD, 128, 256, 256, 128, 2, 8, 4, BF16>;
 template <bool BF16> using Dq256 = Cfg<ROLE_DQ, 128, 256, 256, 128, 1, 6, 2, BF16>;
-template <bool BF16> using Dk256 = PairCfg<ROLE_DK, 256, 128, 2, 8, BF16>;  // pair: faster than 1-CTA here
+template <bool BF16> using Dk256 = PairCfg<ROLE_DK, 256, 128, 2, 4, BF16>;  // pair: faster than 1-CTA here
 template <bool BF16> using Dv256 = Cfg<ROLE_DV, 128, 256, 256, 128, 2, 8, 4, BF16>;
 // head_dim 512: CTA pairs, PairCfg<ROLE, D, BN, NS, NSTAGES, BF16>. The forward keeps all 512 O
 // columns in TMEM (256 per CTA), so S is computed once per item. 256-column items make
 // every score MMA an N=256 pair instruction (full tensor rate; N=128 pair MMAs run at 70%), at the
 // price of single-buffered S/dP in TMEM for dQ and dK (256 + 128 + 128 columns).
-template <bool BF16> using Fwd512 = PairCfg<ROLE_FWD, 512, 256, 2, 6, BF16>;
-template <bool BF16> using Dq512 = PairCfg<ROLE_DQ, 512, 256, 1, 4, BF16>;
-template <bool BF16> using Dk512 = PairCfg<ROLE_DK, 512, 256, 1, 4, BF16>;
-template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 256, 2, 6, BF16>;
+template <bool BF16> using Fwd512 = PairCfg<ROLE_FWD, 512, 256, 2, 3, BF16>;
+template <bool BF16> using Dq512 = PairCfg<ROLE_DQ, 512, 256, 1, 2, BF16>;
+template <bool BF16> using Dk512 = PairCfg<ROLE_DK, 512, 256, 1, 2, BF16>;
+template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 256, 2, 3, BF16>;
 
 // Materialised backward (gqafa_bwd_ws): a pair dQ kernel that also stores P
 // and dS, then the dK + dV kernel. At head_dim 256 the dQ kernel is the
 // pair configuration with 256-key items (the recomputing path keeps the
 // 1-CTA Dq256).
 template <bool BF16> using Dkv512 = DkvCfg<512, 7, BF16>;
-template <bool BF16> using DqWs256 = PairCfg<ROLE_DQ, 256, 256, 1, 8, BF16>;
+template <bool BF16> using DqWs256 = PairCfg<ROLE_DQ, 256, 256, 1, 4, BF16>;
 template <bool BF16> using Dkv256 = DkvCfg<256, 7, BF16>;
 
 struct Problem {
