@@ -202,8 +202,7 @@ def _fwd(q, k, v, causal, window, scale, want_lse, rows=None, out=None):
 def _workspace_limit():
     """Largest backward workspace (bytes) `_bwd` may allocate; GQAFA_BWD_WORKSPACE_LIMIT
     overrides (0 turns the materialised backward off). Default: no limit beyond
-    what the allocator can give; an allocation failure falls back to the
-    recomputing backward."""
+    what the allocator can give."""
     env = os.environ.get("GQAFA_BWD_WORKSPACE_LIMIT")
     return None if env is None else int(env)
 
@@ -235,7 +234,9 @@ def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=
     A full backward (no stage, no rows) takes the materialised
     path (gqafa_bwd_ws: the dQ kernel stores P and dS, one kernel makes dK and
     dV from them) with a workspace from the caching allocator, or `workspace`
-    when given; without the memory it runs the recomputing gqafa_bwd. With a
+    when given; when the whole workspace does not fit (memory or
+    GQAFA_BWD_WORKSPACE_LIMIT) it runs over groups of KV heads, and without
+    room for one KV head's share it runs the recomputing gqafa_bwd. With a
     `workspace` tensor, `stage` 0 / 1 selects that path's kernels instead."""
     lib = _lib.load()
     b, h_q, n, d = q.shape
@@ -250,8 +251,12 @@ def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=
     else:
         dq, dk, dv, delta = out
     ws = workspace
+    chunks = None
     if ws is None and stage is None and rows is None:
-        ws = _alloc_workspace(bwd_workspace_size(b, h_q, h_kv, n, d, causal, window), q.device)
+        size = bwd_workspace_size(b, h_q, h_kv, n, d, causal, window)
+        ws = _alloc_workspace(size, q.device)
+        if ws is None and size > 0:
+            chunks, ws = _workspace_chunks(size, b, h_kv, q.device)
     if ws is not None:
         tail = (ws.data_ptr(), ws.numel() * ws.element_size())
         if stage is None:
@@ -264,22 +269,59 @@ def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=
         fn = lib.gqafa_bwd if stage is None else (lambda *a: lib.gqafa_bwd_stage(int(stage), *a))
     with _DeviceScope(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        rc = fn(
-            q.data_ptr(), _lib.strides_arg(q.stride()),
-            k.data_ptr(), _lib.strides_arg(k.stride()),
-            v.data_ptr(), _lib.strides_arg(v.stride()),
-            o.data_ptr(), _lib.strides_arg(o.stride()),
-            do.data_ptr(), _lib.strides_arg(do.stride()),
-            lse.data_ptr(),
-            dq.data_ptr(), _lib.strides_arg(dq.stride()),
-            dk.data_ptr(), _lib.strides_arg(dk.stride()),
-            dv.data_ptr(), _lib.strides_arg(dv.stride()),
-            delta.data_ptr(),
-            b, h_q, h_kv, n, d, float(scale), 1 if causal else 0, int(window),
-            _DTYPES[q.dtype], stream,
-        )
-    _lib.check(rc)
+        if chunks is None:
+            _lib.check(fn(*_bwd_args(q, k, v, o, do, lse, dq, dk, dv, delta, causal, window, scale, stream)))
+        else:
+            # the materialised backward over groups of `chunks` KV heads of one
+            # batch element (units are independent; every slice is a view)
+            g = h_q // h_kv
+            for bi in range(b):
+                for h0 in range(0, h_kv, chunks):
+                    h1 = min(h_kv, h0 + chunks)
+                    sq, sk, sb = slice(h0 * g, h1 * g), slice(h0, h1), slice(bi, bi + 1)
+                    _lib.check(fn(*_bwd_args(
+                        q[sb, sq], k[sb, sk], v[sb, sk], o[sb, sq], do[sb, sq], lse[sb, sq],
+                        dq[sb, sq], dk[sb, sk], dv[sb, sk], delta[sb, sq], causal, window, scale, stream)))
     return dq, dk, dv
+
+
+def _workspace_chunks(size, b, h_kv, device):
+    """(KV heads per chunk, workspace) for a materialised backward split over
+    groups of KV heads when the whole workspace does not fit; (None, None) if
+    one KV head's share does not fit either (the caller then recomputes). The
+    workspace is linear in B * H_Q, so one KV head of one batch element needs
+    size / (B * H_KV)."""
+    limit = _workspace_limit()
+    if limit == 0:
+        return None, None
+    per_head = size // (b * h_kv)
+    hc = h_kv if b > 1 else h_kv // 2
+    while hc >= 1:
+        ws = _alloc_workspace(per_head * hc, device)
+        if ws is not None:
+            return hc, ws
+        hc //= 2
+    return None, None
+
+
+def _bwd_args(q, k, v, o, do, lse, dq, dk, dv, delta, causal, window, scale, stream):
+    """The gqafa_bwd argument list (without the workspace) for these tensors;
+    lse and delta must be contiguous [B, H_Q, N]."""
+    b, h_q, n, d = q.shape
+    return (
+        q.data_ptr(), _lib.strides_arg(q.stride()),
+        k.data_ptr(), _lib.strides_arg(k.stride()),
+        v.data_ptr(), _lib.strides_arg(v.stride()),
+        o.data_ptr(), _lib.strides_arg(o.stride()),
+        do.data_ptr(), _lib.strides_arg(do.stride()),
+        lse.data_ptr(),
+        dq.data_ptr(), _lib.strides_arg(dq.stride()),
+        dk.data_ptr(), _lib.strides_arg(dk.stride()),
+        dv.data_ptr(), _lib.strides_arg(dv.stride()),
+        delta.data_ptr(),
+        b, h_q, k.shape[1], n, d, float(scale), 1 if causal else 0, int(window),
+        _DTYPES[q.dtype], stream,
+    )
 
 
 # --------------------------------------------------------------------------

@@ -60,3 +60,20 @@ def test_reference_eager_functions_run_on_cpu():
     a = gfa.attention_gqa_ref(q, k, v, causal=True)
     b = gfa.attention_swa_ref(q, k, v, slide_size=24)
     torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-5)
+
+
+def test_workspace_chunk_plan(monkeypatch):
+    """KV heads per chunk of the split materialised backward under a limit
+    (workspace linear in B * H_Q; planner allocates on the given device)."""
+    from gemma_triton_flash_attn.attention import _workspace_chunks
+    size = 2 * 4 * 1000  # B=2, H_KV=4: 1000 bytes per KV head
+    monkeypatch.setenv("GQAFA_BWD_WORKSPACE_LIMIT", str(size // 3))
+    hc, ws = _workspace_chunks(size, 2, 4, "cpu")
+    assert hc == 2 and ws.numel() == 2000
+    monkeypatch.setenv("GQAFA_BWD_WORKSPACE_LIMIT", "1500")
+    hc, ws = _workspace_chunks(size, 2, 4, "cpu")
+    assert hc == 1 and ws.numel() == 1000
+    monkeypatch.setenv("GQAFA_BWD_WORKSPACE_LIMIT", "999")
+    assert _workspace_chunks(size, 2, 4, "cpu") == (None, None)
+    monkeypatch.setenv("GQAFA_BWD_WORKSPACE_LIMIT", "0")
+    assert _workspace_chunks(size, 2, 4, "cpu") == (None, None)

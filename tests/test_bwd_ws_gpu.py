@@ -98,3 +98,20 @@ def test_default_path_uses_workspace_and_limit_env(monkeypatch):
     assert torch.equal(a[0], r[0])
     for x, y in zip(a[1:], r[1:]):
         assert (x.float() - y.float()).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("D", [256, 512])
+def test_workspace_limit_splits_over_kv_heads(monkeypatch, D):
+    """A workspace limit below the whole problem's need runs the materialised
+    backward over groups of KV heads: bitwise the same gradients."""
+    B, Hq, Hkv, N = 2, 8, 4, 384
+    q, k, v, do = (t.to(DEV) for t in make_inputs(B, Hq, Hkv, N, D, seed=7))
+    scale = 1 / math.sqrt(D)
+    o, lse = _fwd(q, k, v, True, 0, scale, True)
+    whole = _bwd(q, k, v, o, lse, do, True, 0, scale)
+    size = bwd_workspace_size(B, Hq, Hkv, N, D, True, 0)
+    monkeypatch.setenv("GQAFA_BWD_WORKSPACE_LIMIT", str(size // 3))  # 2 KV heads per chunk
+    split = _bwd(q, k, v, o, lse, do, True, 0, scale)
+    torch.cuda.synchronize()
+    for x, y in zip(whole, split):
+        assert torch.equal(x, y)
