@@ -133,6 +133,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         ++cnt;
         return true;
       };
+      // P / dS blocks are read once (evict-first); Q and dO tiles are read by
+      // every key tile of the group (evict-last).
+      const uint64_t pol_ws = l2_policy_evict_first(), pol_qdo = l2_policy_evict_last();
       const long long before_lo = ws_blocks_before(t_lo, N, p.causal, p.window);
       for (int g0 = 0; g0 < G && ok; ++g0) {
         const int hq = h * G + g0;
@@ -149,10 +152,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           ok = acquire(st);
           if (!ok) break;
           const uint32_t full_l = mapa_shared(BAR_FULL(st), 0);
-          tma_load_3d_pair(smem_u32(sRing + st * C::STAGE_BYTES), &tmWS, full_l, kcol, 0,
-                           static_cast<int>(p.ws_blocks + blk));
-          tma_load_3d_pair(smem_u32(sRing + st * C::STAGE_BYTES + C::PANEL_BYTES), &tmWS, full_l, kcol, 0,
-                           static_cast<int>(blk));
+          tma_load_3d_pair_hint(smem_u32(sRing + st * C::STAGE_BYTES), &tmWS, full_l, kcol, 0,
+                                static_cast<int>(p.ws_blocks + blk), pol_ws);
+          tma_load_3d_pair_hint(smem_u32(sRing + st * C::STAGE_BYTES + C::PANEL_BYTES), &tmWS, full_l, kcol, 0,
+                                static_cast<int>(blk), pol_ws);
           for (int g = 0; g < C::NACC && ok; ++g) {
             for (int m = 0; m < 2 && ok; ++m) {
               const CUtensorMap* map = (m == 0) ? &tmQ : &tmDO;
@@ -160,8 +163,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
               if (!ok) break;
               const uint32_t fl = mapa_shared(BAR_FULL(st), 0);
               for (int j = 0; j < 2; ++j)
-                tma_load_4d_pair(smem_u32(sRing + st * C::STAGE_BYTES + j * C::PANEL_BYTES), map, fl,
-                                 64 * (4 * g + 2 * static_cast<int>(rank) + j), 128 * t, hq, b);
+                tma_load_4d_pair_hint(smem_u32(sRing + st * C::STAGE_BYTES + j * C::PANEL_BYTES), map, fl,
+                                      64 * (4 * g + 2 * static_cast<int>(rank) + j), 128 * t, hq, b, pol_qdo);
             }
           }
         }

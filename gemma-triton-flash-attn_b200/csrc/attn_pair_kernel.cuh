@@ -27,9 +27,15 @@
 
 namespace gqafa {
 
-template <int ROLE_, int D_, int BN_, int NS_, int NSTAGES_, bool BF16_>
+// RW_ = number of row warpgroups (4 warps each). With RW_ = 2 two warps share
+// every TMEM lane quadrant and split each item's columns between them, so the
+// elementwise work per item (exp2, masking, dS, packing into the P buffer) is
+// spread over twice as many warps.
+template <int ROLE_, int D_, int BN_, int NS_, int NSTAGES_, bool BF16_, int RW_ = 1>
 struct PairCfg {
   static constexpr int ROLE = ROLE_, D = D_, BN = BN_, NS = NS_, NSTAGES = NSTAGES_;
+  static constexpr int RW = RW_;
+  static constexpr int THREADS = 128 + 128 * RW;
   static constexpr bool BF16 = BF16_;
   static constexpr bool PAIR = true;
   static constexpr int M = 64;     // rows per CTA
@@ -63,15 +69,21 @@ struct PairCfg {
   // MMAs, so the tensor pipe works while the row warps form dS.
   static constexpr bool EARLY_S = HAS_DP && NS == 1;
   static constexpr int NBARS = 2 * NSTAGES + 1 + 4 * NS + 2;
-  // sRow (M floats), then for the forward the row-statistics exchange:
-  // [2 slots][2 halves][M] maxima and [2 halves][M] partial sums.
-  static constexpr int XCH_FLOATS = (ROLE == ROLE_FWD) ? 6 * M : 0;
+  // sRow (M floats), then for the forward the row-statistics exchange between
+  // the 2 * RW warps that hold parts of the same rows:
+  // [2 slots][2 * RW parts][M] maxima and [2 * RW parts][M] partial sums.
+  static constexpr int XCH_FLOATS = (ROLE == ROLE_FWD) ? 6 * RW * M : 0;
   static constexpr int MISC_BYTES = M * 4 + XCH_FLOATS * 4 + NBARS * 8 + 16;
   static constexpr int SMEM_BYTES = 1024 + R_BYTES + RING_BYTES + PBUF_BYTES + MISC_BYTES;
   static constexpr int ACC_COLS = D / 2;
   static constexpr int SBUF_COLS = BN / 2;
   static constexpr uint32_t IDESC_S = make_idesc(MP, BN, BF16, false);
   static constexpr uint32_t IDESC_Y = make_idesc(MP, 256, BF16, true);
+  static constexpr int KCH = SBUF_COLS / 32;  // 32-column chunks of an item per TMEM lane
+  static constexpr int KCHW = KCH / RW;       // ... per row warp
+
+  static_assert(RW == 1 || RW == 2, "row warpgroups");
+  static_assert(KCH % RW == 0 && (ACC_COLS / 32) % (2 * RW) == 0 && (NACC * 4) % RW == 0, "column split");
 
   static_assert(D % 256 == 0, "D");
   static_assert(BN == 128 || BN == 256, "BN");
@@ -81,7 +93,7 @@ struct PairCfg {
 };
 
 template <class C>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tmR1, const __grid_constant__ CUtensorMap tmR2,
                      const __grid_constant__ CUtensorMap tmC1, const __grid_constant__ CUtensorMap tmC2,
                      const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmWS,
@@ -166,8 +178,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     for (int s = 0; s < NS; ++s) {
       mbar_init(BAR_SFULL(s), 1);
       mbar_init(BAR_SREADY(s), 1);
-      mbar_init(BAR_SFREE(s), 8);
-      mbar_init(BAR_PREADY(s), 8);  // 4 row warps in each CTA of the pair
+      mbar_init(BAR_SFREE(s), 8 * C::RW);
+      mbar_init(BAR_PREADY(s), 8 * C::RW);  // 4 * RW row warps in each CTA of the pair
     }
     mbar_init(BAR_ACC, 1);
     mbar_init(BAR_FINAL, 1);
@@ -395,10 +407,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     // ======================= row warps (both CTAs) =======================
     // 2x2 TMEM layout: lane l of quadrant q holds row 32*(q%2)+l, and the
     // first (q < 2) or second (q >= 2) half of each N range.
+    // With RW = 2, warps w and w + 4 share a quadrant; `cs` selects which
+    // KCHW of the KCH column chunks (and which part of the epilogue) a warp owns.
+    const int rwi = warp - 4;
     const int q4 = warp & 3;
+    const int cs = rwi >> 2;
     const int half = q4 >> 1;
     const int row = 32 * (q4 & 1) + lane;
     const uint32_t tq = tbase + (static_cast<uint32_t>(q4 * 32) << 16);
+    constexpr int RW = C::RW, KCHW = C::KCHW;
+    const int kc0 = cs * KCHW;  // first column chunk this warp owns
     const float LOG2E = 1.4426950408889634f;
     const float sl2 = p.scale_log2;
     bool ok = true;
@@ -410,7 +428,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     if constexpr (C::ROLE == ROLE_DQ) {
       const uint16_t* Og = reinterpret_cast<const uint16_t*>(p.o) + b * p.o_sb + h * p.o_sh;
       const uint16_t* dOg = reinterpret_cast<const uint16_t*>(p.dout) + b * p.do_sb + h * p.do_sh;
-      for (int r = q4; r < M; r += 4) {
+      for (int r = rwi; r < M; r += 4 * RW) {
         const int q = r0 + r;
         float acc = 0.f;
         if (q < N) {
@@ -433,12 +451,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           if (q < N) p.delta[rowbase_q + q] = acc;
         }
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"n"(128 * C::RW) : "memory");
       row_delta = sRow[row];
       row_lse2 = (r0 + row < N) ? p.lse[rowbase_q + r0 + row] * LOG2E : 0.f;
     }
 
-    constexpr int KCH = C::SBUF_COLS / 32;  // 32-column chunks this thread owns per item
     // Materialised backward (dQ role): workspace block of item 0 of this
     // (b, h, q tile); item i is block ws_blk0 + i, its dS block ws_blocks later.
     long long ws_blk0 = 0;
@@ -455,7 +472,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       // barrier runs on every item even after a failed wait, so a partner warp
       // is never left at it.
       const int pbar = 2 + (q4 & 1);
-      auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(pbar) : "memory"); };
+      const int part = half * RW + cs;  // which part of the row's columns this warp holds
+      auto pair_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(pbar), "n"(64 * C::RW) : "memory"); };
       float m_run = -INFINITY, l_run = 0.f;
       for (int i = 0; i < n_items; ++i) {
         const int sb = i % NS;
@@ -481,7 +499,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         if (ok) {
           tc_fence_after();
 #pragma unroll 1
-          for (int kb = 0; kb < KCH; kb += 2) {
+          for (int kb = kc0; kb < kc0 + KCHW; kb += 2) {
             uint32_t rs[2][32];
             tmem_ld32_async(tq + s_col + 32 * kb, rs[0]);
             tmem_ld32_async(tq + s_col + 32 * (kb + 1), rs[1]);
@@ -499,10 +517,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           }
           mx *= sl2;  // sl2 > 0, so the max commutes with the scaling
         }
-        float* xm = sX + (i & 1) * 2 * M;
-        xm[half * M + row] = mx;
+        float* xm = sX + (i & 1) * 2 * RW * M;
+        xm[part * M + row] = mx;
         pair_sync();
-        mx = fmaxf(mx, xm[(half ^ 1) * M + row]);
+#pragma unroll
+        for (int pt = 0; pt < 2 * RW; ++pt) mx = fmaxf(mx, xm[pt * M + row]);
         if (!ok) continue;
         float alpha = 1.f;
         bool rescale = false;
@@ -517,7 +536,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const float ms = (m_run == -INFINITY) ? 0.f : m_run;
         float sum = 0.f;
 #pragma unroll 1
-        for (int k = 0; k < KCH; ++k) {
+        for (int k = kc0; k < kc0 + KCHW; ++k) {
           uint32_t r[32];
           tmem_ld32(tq + s_col + 32 * k, r);
           float e[32];
@@ -551,7 +570,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           if (!ok) continue;
           tc_fence_after();
 #pragma unroll 1
-          for (int k = 0; k < C::ACC_COLS / 32; k += 2) {
+          for (int k = cs * (C::ACC_COLS / 32 / RW); k < (cs + 1) * (C::ACC_COLS / 32 / RW); k += 2) {
             uint32_t r[2][32];
             tmem_ld32_async(tq + 32 * k, r[0]);
             tmem_ld32_async(tq + 32 * (k + 1), r[1]);
@@ -575,10 +594,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
 
       // ---------------- epilogue ----------------
       const long long t_epi = tick();
-      float* xl = sX + 4 * M;
-      xl[half * M + row] = l_run;
+      float* xl = sX + 4 * RW * M;
+      xl[part * M + row] = l_run;
       pair_sync();
-      const float l_tot = l_run + xl[(half ^ 1) * M + row];
+      float l_tot = 0.f;
+#pragma unroll
+      for (int pt = 0; pt < 2 * RW; ++pt) l_tot += xl[pt * M + row];
       if (ok && n_items > 0) {
         ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
         ok = __all_sync(0xffffffffu, ok);
@@ -590,9 +611,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const long long obase = static_cast<long long>(b) * p.out_sb + static_cast<long long>(h) * p.out_sh +
                                 static_cast<long long>(orow) * p.out_sn;
 #pragma unroll 1
-        for (int g = 0; g < C::NACC; ++g) {
-#pragma unroll 1
-          for (int k = 0; k < 4; ++k) {
+        for (int e = cs * (4 * C::NACC / RW); e < (cs + 1) * (4 * C::NACC / RW); ++e) {
+          const int g = e >> 2, k = e & 3;
+          {
             uint32_t r[32];
             tmem_ld32(tq + g * 128 + 32 * k, r);
             float v[32];
@@ -601,7 +622,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             if (orow < N) store_row32<C::BF16>(p.out, obase + 256 * g + 128 * half + 32 * k, v);
           }
         }
-        if (p.lse != nullptr && half == 0 && orow < N) {
+        if (p.lse != nullptr && part == 0 && orow < N) {
           const float LN2 = 0.6931471805599453f;
           p.lse[rowbase_q + orow] = (l_tot > 0.f) ? (m_run + __log2f(l_tot)) * LN2 : -INFINITY;
         }
@@ -616,7 +637,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       // still reaches every barrier.
       const bool ws_on = (C::ROLE == ROLE_DQ && BN == 256) && p.ws != nullptr;
       const bool tid0 = (warp == 4 && lane == 0);
-      auto row_bar = [&]() { asm volatile("bar.sync 1, 128;" ::: "memory"); };
+      auto row_bar = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(128 * C::RW) : "memory"); };
       // K-major SWIZZLE_128B [64 rows x BN] tile of 64-column panels.
       auto put = [&](int sb, int k, const float (&vals)[32]) {
         const int col = half * (BN / 2) + 32 * k;  // column within the item
@@ -632,11 +653,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (row & 7)) * 16)) = w;
         }
       };
+      // The workspace is read once, by the dK/dV kernel: store it evict-first.
+      const uint64_t ws_pol = l2_policy_evict_first();
       auto store_block = [&](int sb, long long blk) {
 #pragma unroll
         for (int c = 0; c < BN / 64; ++c)
-          tma_store_3d(&tmWS, smem_u32(sP + sb * C::PBUF_ONE + c * (M * 128)), 64 * c, M * static_cast<int>(rank),
-                       static_cast<int>(blk));
+          tma_store_3d_hint(&tmWS, smem_u32(sP + sb * C::PBUF_ONE + c * (M * 128)), 64 * c,
+                            M * static_cast<int>(rank), static_cast<int>(blk), ws_pol);
         bulk_commit();
       };
       for (int i = 0; i < n_items; ++i) {
@@ -645,13 +668,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const int cb = c0 + half * (BN / 2);  // first column this thread owns
         // Per-column softmax statistics (DK / DV), fetched before waiting so the
         // global-load latency overlaps the MMAs.
-        float col_lse2[KCH], col_delta[KCH];
+        float col_lse2[KCHW], col_delta[KCHW];
         if constexpr (!C::ROWS_ARE_Q) {
           const int hq = item_headC(i);
           const long long colbase = (static_cast<long long>(b) * p.Hq + hq) * N;
 #pragma unroll
-          for (int k = 0; k < KCH; ++k) {
-            const int qq = cb + 32 * k + lane;
+          for (int k = 0; k < KCHW; ++k) {
+            const int qq = cb + 32 * (kc0 + k) + lane;
             col_lse2[k] = (qq < N) ? p.lse[colbase + qq] * LOG2E : 0.f;
             col_delta[k] = (C::HAS_DP && qq < N) ? p.delta[colbase + qq] : 0.f;
           }
@@ -667,9 +690,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const long long t_work = tick();
         const uint32_t s_col = C::ACC_COLS + sb * C::SBUF_COLS;
         const uint32_t dp_col = C::ACC_COLS + (NS + sb) * C::SBUF_COLS;
-        constexpr int KB = KCH < 2 ? KCH : 2;  // chunks loaded per TMEM round trip (register budget)
-        // P = exp2(S * scale * log2 e - lse * log2 e), masked, for all columns this thread owns.
-        float pv[KCH][32];
+        constexpr int KB = KCHW < 2 ? KCHW : 2;  // chunks loaded per TMEM round trip (register budget)
+        // P = exp2(S * scale * log2 e - lse * log2 e), masked, for all columns this thread owns
+        // (local chunk k is column chunk kc0 + k of the item).
+        float pv[KCHW][32];
         if (ok) {
           tc_fence_after();
           int lo_abs, hi_abs;
@@ -677,10 +701,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           const int lo_rel = lo_abs - cb;
           const unsigned span = span_of(lo_rel, hi_abs - cb);
 #pragma unroll
-          for (int kb = 0; kb < KCH; kb += KB) {
+          for (int kb = 0; kb < KCHW; kb += KB) {
             uint32_t rs[KB][32];
 #pragma unroll
-            for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + s_col + 32 * (kb + u), rs[u]);
+            for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + s_col + 32 * (kc0 + kb + u), rs[u]);
 #pragma unroll
             for (int u = 0; u < KB; ++u) tmem_ld_wait32(rs[u]);
 #pragma unroll
@@ -690,7 +714,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
               for (int j = 0; j < 32; ++j) {
                 const float l2 = C::ROWS_ARE_Q ? row_lse2 : __shfl_sync(0xffffffffu, col_lse2[k], j);
                 const float e = ex2(__uint_as_float(rs[u][j]) * sl2 - l2);
-                pv[k][j] = (static_cast<unsigned>(32 * k + j - lo_rel) < span) ? e : 0.f;
+                pv[k][j] = (static_cast<unsigned>(32 * (kc0 + k) + j - lo_rel) < span) ? e : 0.f;
               }
             }
           }
@@ -714,7 +738,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           row_bar();
           if (ok) {
 #pragma unroll
-            for (int k = 0; k < KCH; ++k) put(sb, k, pv[k]);
+            for (int k = 0; k < KCHW; ++k) put(sb, kc0 + k, pv[k]);
             fence_proxy_async_smem();
           }
           row_bar();
@@ -731,11 +755,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         }
         if (ok) {
 #pragma unroll
-          for (int kb = 0; kb < KCH; kb += KB) {
+          for (int kb = 0; kb < KCHW; kb += KB) {
             uint32_t rd[KB][32];
             if constexpr (C::HAS_DP) {
 #pragma unroll
-              for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + dp_col + 32 * (kb + u), rd[u]);
+              for (int u = 0; u < KB; ++u) tmem_ld32_async(tq + dp_col + 32 * (kc0 + kb + u), rd[u]);
 #pragma unroll
               for (int u = 0; u < KB; ++u) tmem_ld_wait32(rd[u]);
             }
@@ -752,7 +776,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                   v[j] = pv[k][j];
                 }
               }
-              put(sb, k, v);
+              put(sb, kc0 + k, v);
             }
           }
           tc_fence_before();
@@ -783,9 +807,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const long long obase = static_cast<long long>(b) * p.out_sb + static_cast<long long>(h) * p.out_sh +
                                 static_cast<long long>(orow) * p.out_sn;
 #pragma unroll 1
-        for (int g = 0; g < C::NACC; ++g) {
-#pragma unroll 1
-          for (int k = 0; k < 4; ++k) {
+        for (int e = cs * (4 * C::NACC / RW); e < (cs + 1) * (4 * C::NACC / RW); ++e) {
+          const int g = e >> 2, k = e & 3;
+          {
             uint32_t r[32];
             tmem_ld32(tq + g * 128 + 32 * k, r);
             float v[32];

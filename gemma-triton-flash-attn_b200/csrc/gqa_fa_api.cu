@@ -167,7 +167,7 @@ int launch(const CUtensorMap (&maps)[6], KParams p, cudaStream_t stream) {
   const long long grid = (long long)p.num_row_tiles * heads * p.B * C::NCHUNK * (C::PAIR ? 2 : 1);
   if (grid <= 0 || grid > 0x7fffffffLL) return fail(GQAFA_ERR_INVALID, "grid size %lld out of range", grid);
   if constexpr (C::PAIR) {
-    attn_pair_kernel<C><<<(unsigned)grid, 256, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3],
+    attn_pair_kernel<C><<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3],
                                                                          maps[4], maps[5], p);
   } else {
     attn_kernel<C><<<(unsigned)grid, 256, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], p);
@@ -187,7 +187,7 @@ template <bool BF16> using Dv256 = Cfg<ROLE_DV, 128, 256, 256, 128, 2, 8, 4, BF1
 // every score MMA an N=256 pair instruction (full tensor rate; N=128 pair MMAs run at 70%), at the
 // price of single-buffered S/dP in TMEM for dQ and dK (256 + 128 + 128 columns).
 template <bool BF16> using Fwd512 = PairCfg<ROLE_FWD, 512, 256, 2, 3, BF16>;
-template <bool BF16> using Dq512 = PairCfg<ROLE_DQ, 512, 256, 1, 2, BF16>;
+template <bool BF16> using Dq512 = PairCfg<ROLE_DQ, 512, 256, 1, 2, BF16, 2>;
 template <bool BF16> using Dk512 = PairCfg<ROLE_DK, 512, 256, 1, 2, BF16>;
 template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 256, 2, 3, BF16>;
 
@@ -196,7 +196,7 @@ template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 256, 2, 3, BF16>;
 // pair configuration with 256-key items (the recomputing path keeps the
 // 1-CTA Dq256).
 template <bool BF16> using Dkv512 = DkvCfg<512, 7, BF16>;
-template <bool BF16> using DqWs256 = PairCfg<ROLE_DQ, 256, 256, 1, 4, BF16>;
+template <bool BF16> using DqWs256 = PairCfg<ROLE_DQ, 256, 256, 1, 4, BF16, 2>;
 template <bool BF16> using Dkv256 = DkvCfg<256, 7, BF16>;
 
 struct Problem {
