@@ -1,25 +1,34 @@
 #!/usr/bin/env python
 """Headline benchmark: GQA flash-attention TFLOPS/s on B200.
 
-Workload (the north-star shape): Gemma-4-E2B global layer,
-B=1 per GPU, H_Q=32, H_KV=4, D=512, causal, N=16384, bf16, inputs seeded
+One GPU (the default): BASELINE config 2, the north-star shape: Gemma-4-E2B
+global layer, B=1, H_Q=32, H_KV=4, D=512, causal, N=16384, bf16, inputs seeded
 N(0,1)*0.5. One step = one forward + backward through the public autograd API
-(FlashAttnGQAFunction: 1 forward launch + 3 backward launches). FLOPs are
-charged by the reference's convention (fwd+bwd = 7*B*H*N^2*D).
+(FlashAttnGQAFunction: 1 forward launch, then the materialised backward's dQ +
+P/dS launch and dK + dV launch). FLOPs are charged by the reference's
+convention (fwd+bwd = 7*B*H*N^2*D, window-limited for a sliding window).
+
+N > 1 GPUs (torchrun, one rank per GPU): BASELINE config 4 as one fixed
+problem (strong scaling): B=4, H_Q=16, H_KV=2, D=512, causal, N=16384, bf16.
+Its 8 (batch, KV-head) units are spread over the ranks in equal blocks, each
+rank computes whole units, and NCCL all-gathers reassemble O, LSE, dQ, dK and
+dV on every rank inside the timed step (sharding.UnitShardedAttention; the O
+gather overlaps the backward kernels, the dQ gather the dK/dV kernels).
+`--scaling weak` instead runs config 2 with one batch element per rank and no
+collective. The one-GPU line carries config 4 on one GPU (`cfg4_1gpu`) as the
+strong-scaling reference.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 runs under torchrun, one rank per GPU: weak scaling, each rank owns one
-batch element, i.e. the (b, kv-head-group) units of b = rank; there is no
-collective on the data path (the units are independent), so the timed region
-holds no communication. Timing: CUDA events on the launching stream, barrier +
-synchronize around the K timed steps, max over ranks. Q/dO are 512 MiB each,
-larger than the 126 MB L2, so no flush is needed between steps.
+Timing: W warm-up steps, then K steps between barrier + synchronize, CUDA
+events on the launching stream, max over ranks. Q/dO are 512 MiB each (1 GiB
+at config 4), larger than the 126 MB L2, so no flush is needed between steps.
 
-`--impl reference` times the reference algorithm's CPU restatement (the
-oracle port; the reference itself is Python + Triton and has no native CPU
-path of its own beyond PyTorch eager) on this host's cores, on bounded
-samples of the same workload.
+CPU legs (`cpu_baseline`, `--impl reference`): the reference's own CPU path
+for this math, its eager `attention_gqa_ref` (expand KV heads + torch SDPA in
+fp32, autograd backward; restated in oracle/eager_ref.py), on all host cores,
+on a bounded sample of the same workload (2 query heads of one KV group at the
+full N=16384), plus BASELINE config 1 whole (B=1, 32/4, N=512, D=512, fp32).
 """
 from __future__ import annotations
 
@@ -61,14 +70,15 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
+                    help="default: cfg2 on one GPU, cfg4 (strong scaling) on several")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="N > 1: strong = one config-4 problem over the GPUs with all-gathers (default); "
+                         "weak = config 2 per GPU, no collective")
     ap.add_argument("--seqlen", type=int, default=None, help="override N (not the headline)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="target CPU seconds per sample")
-    ap.add_argument("--strong", action="store_true",
-                    help="strong scaling: one config-2 problem (B=1) split over the GPUs by (batch, KV-group) units, "
-                         "and by sequence blocks when there are more GPUs than units; outputs all-gathered")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the per-config sweep of the one-GPU line")
     ap.add_argument("--only", choices=["fwd", "dq", "dk", "dv", "dqps", "dkv"], default=None,
                     help="profiling mode: run only this kernel, warmup + steps launches, print nothing")
     return ap.parse_args()
@@ -215,60 +225,67 @@ def max_over_ranks(x, world, device):
     return t.item()
 
 
-# ------------------------------------------------------------------ CPU leg
-def cpu_sample_run(wl, rows, seed=0):
-    """fwd+bwd of the oracle port on query head 0 of batch 0, query rows
-    [N-rows, N) against all keys (the heaviest causal rows). Returns
-    (seconds, charged FLOPs of the sample)."""
-    import numpy as np
+# ------------------------------------------------------------------ CPU legs
+CPU_SAMPLE_HEADS = 1
 
-    from oracle.attention_oracle import attention_bwd, attention_fwd
 
-    N, D = wl["N"], wl["D"]
+def cpu_eager_sample(wl, seed=0, warmup=1, reps=3):
+    """The reference's eager CPU path (oracle/eager_ref.py) on a bounded sample
+    of `wl`: query heads 0 .. CPU_SAMPLE_HEADS-1 of batch 0 (both in KV group
+    0) with their KV head, at the full sequence length, fp32 forward +
+    autograd backward. Returns (median seconds, charged FLOPs, threads, text)."""
+    from gemma_triton_flash_attn.flops import attn_flops
+    from oracle.eager_ref import time_fwd_bwd, use_all_cores
+
+    threads = use_all_cores()
+    N, D, causal = wl["N"], wl["D"], wl["causal"]
+    window = wl["W"] if (causal and 0 < wl["W"] < N) else 0
+    hq = min(CPU_SAMPLE_HEADS, wl["Hq"] // wl["Hkv"])
     g = torch.Generator().manual_seed(seed)
-    mk = lambda *s: (torch.randn(*s, generator=g) * wl["factor"]).to(wl["dtype"]).float().numpy()  # noqa: E731
-    q = mk(1, 1, rows, D)
-    k = mk(1, 1, N, D)
-    v = mk(1, 1, N, D)
-    do = mk(1, 1, rows, D)
-    off = N - rows
-    t0 = time.perf_counter()
-    o, lse = attention_fwd(q, k, v, wl["causal"], wl["W"], q_offset=off, chunk=256)
-    attention_bwd(q, k, v, o, lse, do, wl["causal"], wl["W"], q_offset=off, chunk=256)
-    dt = time.perf_counter() - t0
-    W = wl["W"]
-    pairs = 0
-    for qpos in range(off, N):
-        lo = max(0, qpos - W + 1) if (wl["causal"] and W) else 0
-        hi = qpos + 1 if wl["causal"] else N
-        pairs += hi - lo
-    del np
-    return dt, 14 * D * pairs
+    mk = lambda *s: (torch.randn(*s, generator=g) * wl["factor"]).to(wl["dtype"]).float()  # noqa: E731
+    q, k, v, do = mk(1, hq, N, D), mk(1, 1, N, D), mk(1, 1, N, D), mk(1, hq, N, D)
+    t = time_fwd_bwd(q, k, v, do, causal, window, warmup=warmup, reps=reps)
+    fl = attn_flops(1, hq, N, D, causal, window, bwd=True)
+    text = (f"reference eager path (KV heads repeated + torch SDPA, fp32, autograd backward; oracle/eager_ref.py) "
+            f"on {threads} threads: fwd+bwd of query heads 0-{hq - 1} of KV group 0 at N={N}, D={D}"
+            + (f", window {window}" if window else "") + f"; median of {reps} after {warmup} warm-up")
+    return t, fl, threads, text
 
 
-def cpu_calibrate(wl, target_s):
-    cpu_sample_run(wl, 256)  # warm the BLAS thread pool and allocator
-    t, _ = cpu_sample_run(wl, 256)
-    rows = int(256 * target_s / max(t, 1e-3))
-    rows = max(64, min(wl["N"], rows // 64 * 64))
-    return rows
+def cpu_config1(warmup=3, reps=9):
+    """BASELINE config 1 whole: fp32, B=1, H_Q=32, H_KV=4, N=512, D=512, causal,
+    N(0,1) inputs; fwd and fwd+bwd medians of the reference's eager path."""
+    from oracle.eager_ref import time_fwd_bwd, use_all_cores
+
+    threads = use_all_cores()
+    g = torch.Generator().manual_seed(0)
+    q, k, v, do = (torch.randn(s, generator=g) for s in ((1, 32, 512, 512), (1, 4, 512, 512), (1, 4, 512, 512),
+                                                         (1, 32, 512, 512)))
+    t_fwd = time_fwd_bwd(q, k, v, do, True, warmup=warmup, reps=reps, fwd_only=True)
+    t_all = time_fwd_bwd(q, k, v, do, True, warmup=warmup, reps=reps)
+    fl = 32 * 512 * 512 * 512
+    return dict(fwd_ms=round(t_fwd * 1e3, 2), fwd_tflops=round(2 * fl / t_fwd / 1e12, 4),
+                fwd_bwd_ms=round(t_all * 1e3, 2), fwd_bwd_tflops=round(7 * fl / t_all / 1e12, 4),
+                threads=threads, cpu=_cpu_model(), method=f"median of {reps} after {warmup} warm-up")
 
 
-def cpu_baseline(wl, target_s, steps=1):
-    rows = cpu_calibrate(wl, target_s)
-    vals = []
-    for s in range(steps):
-        dt, fl = cpu_sample_run(wl, rows, seed=s)
-        vals.append(fl / dt / 1e12)
-    cores = os.cpu_count()
-    return dict(value=statistics.median(vals), unit="TFLOPS/s", cores=cores, kind="port",
-                sample=(f"oracle port (numpy fp32, {cores} BLAS threads): fwd+bwd of query head 0, "
-                        f"the last {rows} query rows of N={wl['N']} (D={wl['D']}) against all keys; "
-                        f"FLOPs charged 14*D*attended pairs"),
-                values=vals, rows=rows)
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
 
 
-# ------------------------------------------------------------------ GPU leg
+def cpu_baseline(wl):
+    t, fl, threads, text = cpu_eager_sample(wl)
+    return dict(value=round(fl / t / 1e12, 5), unit="TFLOPS/s", cores=threads, kind="port", sample=text,
+                ms_per_sample=round(t * 1e3, 1), config1=cpu_config1())
+
+
+# ------------------------------------------------------------------ GPU helpers
 def make_inputs(wl, seed, device):
     g = torch.Generator(device=device).manual_seed(seed)
     B, Hq, Hkv, N, D = wl["B"], wl["Hq"], wl["Hkv"], wl["N"], wl["D"]
@@ -291,66 +308,120 @@ def time_loop(fn, steps, stream):
     return start.elapsed_time(end) / steps
 
 
-def run_ours(args, wl, world, rank, local):
-    from gemma_triton_flash_attn import FlashAttnGQAFunction, _lib
-    from gemma_triton_flash_attn.attention import _alloc_workspace, _bwd, _fwd, bwd_workspace_size
-    from gemma_triton_flash_attn.flops import attn_flops, kernel_flops
+def _window(wl):
+    return wl["W"] if (wl["causal"] and 0 < wl["W"] < wl["N"]) else 0
 
-    def _bwd_workspace(*shape_args):
-        # the same workspace decision the public API's backward makes
-        return _alloc_workspace(bwd_workspace_size(*shape_args[:-1]), shape_args[-1])
 
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    stream = torch.cuda.current_stream(device)
-    B, Hq, Hkv, N, D, causal, W = (wl[x] for x in ("B", "Hq", "Hkv", "N", "D", "causal", "W"))
-    window = W if (causal and 0 < W < N) else 0
-    scale = 1.0 / math.sqrt(D)
-    q, k, v, do = make_inputs(wl, 1234 + rank, device)
+def _uuid(device):
+    u = str(torch.cuda.get_device_properties(device).uuid)
+    return [u if u.startswith("GPU-") else "GPU-" + u]
+
+
+def train_step_fn(q, k, v, do, causal, W):
+    from gemma_triton_flash_attn import FlashAttnGQAFunction
+
     qg, kg, vg = (t.detach().requires_grad_(True) for t in (q, k, v))
-    if args.only:
-        o, lse = _fwd(q, k, v, causal, window, scale, True)
-        bufs = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
-                torch.empty((B, Hq, N), dtype=torch.float32, device=device))
-        ws = None
-        if args.only in ("dqps", "dkv"):
-            ws = _bwd_workspace(B, Hq, Hkv, N, D, causal, window, device)
-            if ws is None:
-                raise SystemExit("--only %s: no materialised backward for this workload" % args.only)
-            _bwd(q, k, v, o, lse, do, causal, window, scale, stage=0, out=bufs, workspace=ws)
-        elif args.only != "fwd":
-            _bwd(q, k, v, o, lse, do, causal, window, scale, stage=0, out=bufs)  # delta for dK
-        torch.cuda.synchronize()
-        stage = {"dq": 0, "dk": 1, "dv": 2, "dqps": 0, "dkv": 1}.get(args.only)
-        for _ in range(args.warmup + args.steps):
-            if stage is None:
-                _fwd(q, k, v, causal, window, scale, True)
-            else:
-                _bwd(q, k, v, o, lse, do, causal, window, scale, stage=stage, out=bufs, workspace=ws)
-        torch.cuda.synchronize()
-        if _lib.device_status(local) != 0:
-            raise RuntimeError("kernel status word set")
-        return
 
     def step():
         qg.grad = kg.grad = vg.grad = None
         out = FlashAttnGQAFunction.apply(qg, kg, vg, causal, W)
         out.backward(do)
 
+    return step
+
+
+def measure_config(wl, device, stream, warmup=2, steps=3, seed=1234):
+    """fwd and fwd+bwd of one workload through the public API: ms and TFLOPS/s."""
+    from gemma_triton_flash_attn.attention import _fwd
+    from gemma_triton_flash_attn.flops import attn_flops
+
+    q, k, v, do = make_inputs(wl, seed, device)
+    causal, W, window = wl["causal"], wl["W"], _window(wl)
+    scale = 1.0 / math.sqrt(wl["D"])
+    step = train_step_fn(q, k, v, do, causal, W)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    ms = time_loop(step, steps, stream)
+    f = lambda: _fwd(q, k, v, causal, window, scale, True)  # noqa: E731
+    f()
+    torch.cuda.synchronize()
+    ms_f = time_loop(f, max(steps, 5), stream)
+    B, Hq, N, D = wl["B"], wl["Hq"], wl["N"], wl["D"]
+    res = dict(N=N, D=D, H_Q=Hq, H_KV=wl["Hkv"], B=B, window=window,
+               dtype="bf16" if wl["dtype"] == torch.bfloat16 else "fp16",
+               fwd_ms=round(ms_f, 3), fwd_tflops=round(attn_flops(B, Hq, N, D, causal, window) / ms_f / 1e9, 1),
+               fwd_bwd_ms=round(ms, 3),
+               fwd_bwd_tflops=round(attn_flops(B, Hq, N, D, causal, window, bwd=True) / ms / 1e9, 1))
+    del q, k, v, do, step
+    torch.cuda.empty_cache()
+    return res
+
+
+# ------------------------------------------------------------------ profiling mode
+def run_only(args, wl, local):
+    """Run one kernel (warmup + steps launches) for ncu; prints nothing."""
+    from gemma_triton_flash_attn import _lib
+    from gemma_triton_flash_attn.attention import _alloc_workspace, _bwd, _fwd, bwd_workspace_size
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    B, Hq, Hkv, N, D, causal = (wl[x] for x in ("B", "Hq", "Hkv", "N", "D", "causal"))
+    window = _window(wl)
+    scale = 1.0 / math.sqrt(D)
+    q, k, v, do = make_inputs(wl, 1234, device)
+    o, lse = _fwd(q, k, v, causal, window, scale, True)
+    bufs = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
+            torch.empty((B, Hq, N), dtype=torch.float32, device=device))
+    ws = None
+    if args.only in ("dqps", "dkv"):
+        ws = _alloc_workspace(bwd_workspace_size(B, Hq, Hkv, N, D, causal, window), device)
+        if ws is None:
+            raise SystemExit("--only %s: no materialised backward for this workload" % args.only)
+        _bwd(q, k, v, o, lse, do, causal, window, scale, stage=0, out=bufs, workspace=ws)
+    elif args.only != "fwd":
+        _bwd(q, k, v, o, lse, do, causal, window, scale, stage=0, out=bufs)  # delta for dK
+    torch.cuda.synchronize()
+    stage = {"dq": 0, "dk": 1, "dv": 2, "dqps": 0, "dkv": 1}.get(args.only)
+    for _ in range(args.warmup + args.steps):
+        if stage is None:
+            _fwd(q, k, v, causal, window, scale, True)
+        else:
+            _bwd(q, k, v, o, lse, do, causal, window, scale, stage=stage, out=bufs, workspace=ws)
+    torch.cuda.synchronize()
+    if _lib.device_status(local) != 0:
+        raise RuntimeError("kernel status word set")
+
+
+# ------------------------------------------------------------------ one GPU (and weak scaling)
+def run_single(args, wl, world, rank, local):
+    from gemma_triton_flash_attn import FlashAttnGQAFunction, _lib
+    from gemma_triton_flash_attn.attention import _alloc_workspace, _bwd, _fwd, bwd_workspace_size
+    from gemma_triton_flash_attn.flops import attn_flops, kernel_flops
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(device)
+    B, Hq, Hkv, N, D, causal, W = (wl[x] for x in ("B", "Hq", "Hkv", "N", "D", "causal", "W"))
+    window = _window(wl)
+    scale = 1.0 / math.sqrt(D)
+    q, k, v, do = make_inputs(wl, 1234 + rank, device)
+    step = train_step_fn(q, k, v, do, causal, W)
     flops_step = attn_flops(B, Hq, N, D, causal, window, bwd=True)
     flops_fwd = attn_flops(B, Hq, N, D, causal, window)
 
+    torch.cuda.reset_peak_memory_stats(device)
+    base_mem = torch.cuda.memory_allocated(device)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     barrier(world)
-    uuid = str(torch.cuda.get_device_properties(device).uuid)
-    uuids = [uuid if uuid.startswith("GPU-") else "GPU-" + uuid]
-    with ClockSampler(uuids) as clocks:
+    with ClockSampler(_uuid(device)) as clocks:
         torch.cuda.synchronize()
         barrier(world)
         ms = time_loop(step, args.steps, stream)
         barrier(world)
+    peak_gb = (torch.cuda.max_memory_allocated(device) - base_mem) / 1e9
     ms_max = max_over_ranks(ms, world, device)
     value = world * flops_step / (ms_max * 1e-3) / 1e12
 
@@ -368,7 +439,7 @@ def run_ours(args, wl, world, rank, local):
     bufs = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
             torch.empty((B, Hq, N), dtype=torch.float32, device=device))
     kernels = {"fwd": ms_fwd}
-    ws = _bwd_workspace(B, Hq, Hkv, N, D, causal, window, device)
+    ws = _alloc_workspace(ws_bytes, device)
     if ws is not None:  # materialised backward: dQ (+ P, dS stores), then dK + dV
         names = ("dqps", "dkv")
         mk = lambda st: (lambda: _bwd(q, k, v, o, lse, do, causal, window, scale, stage=st, out=bufs,  # noqa: E731
@@ -392,12 +463,32 @@ def run_ours(args, wl, world, rank, local):
     if os.path.exists(tpath):
         with open(tpath) as f:
             traffic = json.load(f).get(f"{args.workload}:{dom}")
-    roofline = dict(bound="tensor", kernel=dom, achieved=round(achieved, 1), peak=peaks["tflops_sustained"],
-                    unit="TFLOP/s", frac=round(achieved / peaks["tflops_sustained"], 4), traffic=traffic,
-                    peak_kind=f"bf16_tflops_sustained ({peaks['source']}); burst {peaks['tflops_burst']}",
+    burst, sust = peaks["tflops_burst"], peaks["tflops_sustained"]
+    roofline = dict(bound="tensor", kernel=dom, achieved=round(achieved, 1), peak=burst, unit="TFLOP/s",
+                    frac=round(achieved / burst, 4), traffic=traffic,
+                    peak_kind=f"bf16_tflops burst ({peaks['source']}): the kernel is timed alone in a sub-second loop",
+                    frac_of_sustained=round(achieved / sust, 4), sustained_peak=sust,
+                    step_frac=round(value / world / burst, 4),
                     flops_per_launch=kflops, ms_per_launch=round(kernels[dom], 3),
                     kernel_ms={k_: round(v_, 3) for k_, v_ in kernels.items()},
                     kernel_share={k_: round(v_ / sum(kernels.values()), 3) for k_, v_ in kernels.items()})
+
+    # the recomputing backward (no workspace): what the memory fallback runs
+    recompute = None
+    if world == 1 and not args.no_sweep:
+        os.environ["GQAFA_BWD_WORKSPACE_LIMIT"] = "0"
+        try:
+            torch.cuda.reset_peak_memory_stats(device)
+            base = torch.cuda.memory_allocated(device)
+            step()
+            torch.cuda.synchronize()
+            ms_r = time_loop(step, 3, stream)
+            recompute = dict(value=round(flops_step / (ms_r * 1e-3) / 1e12, 2), unit="TFLOPS/s",
+                             ms_per_step=round(ms_r, 3),
+                             peak_mem_gb=round((torch.cuda.max_memory_allocated(device) - base) / 1e9, 3),
+                             kernels="fwd + dQ(+delta) + dK + dV, recomputing S and dP")
+        finally:
+            del os.environ["GQAFA_BWD_WORKSPACE_LIMIT"]
 
     # end to end through the public API with host buffers. Every step uploads
     # its own q, k, v, dO from pinned host memory and downloads dQ, dK, dV;
@@ -451,11 +542,28 @@ def run_ours(args, wl, world, rank, local):
         e2e = dict(value=round(world * flops_step / (ms_e2e * 1e-3) / 1e12, 2), unit="TFLOPS/s",
                    ms_per_step=round(ms_e2e, 3), h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
                    pipeline="copy streams; step s+1 upload and step s download overlap kernels")
+        del host_in, host_out, dev_in
+
+    del q, k, v, do, step, o, lse, bufs
+    torch.cuda.empty_cache()
+
+    # the other configurations of the reference's sweep, through the same API
+    sweep, cfg4 = None, None
+    if world == 1 and not args.no_sweep and args.workload == "cfg2" and args.seqlen is None:
+        sweep = []
+        variants = [("cfg2", dict(N=1024), 20), ("cfg2", dict(N=4096), 5), ("cfg2", dict(N=32768), 2),
+                    ("cfg2", dict(dtype=torch.float16), 3), ("cfg3", dict(), 10), ("cfg3", dict(N=32768), 5)]
+        for name, over, nsteps in variants:
+            w = dict(WORKLOADS[name])
+            w.update(over)
+            r = measure_config(w, device, stream, steps=nsteps)
+            r["workload"] = name
+            sweep.append(r)
+        cfg4 = run_cfg4_one_gpu(device, stream, steps=3)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(wl, args.cpu_seconds, steps=1)
-        cpu.pop("values", None)
+        cpu = cpu_baseline(wl)
 
     if rank == 0:
         line = dict(
@@ -464,13 +572,152 @@ def run_ours(args, wl, world, rank, local):
             vs_baseline=None, dtype="bf16" if wl["dtype"] == torch.bfloat16 else "fp16",
             data="synthetic (seeded N(0,1)*%g, per-rank seed)" % wl["factor"],
             config=dict(workload=wl["name"], B_per_gpu=B, H_Q=Hq, H_KV=Hkv, N=N, D=D, causal=causal,
-                        window=window, global_batch=B * world, seq_len=N, parallelism=f"(b,kv-group) units, dp{world}",
+                        window=window, global_batch=B * world, seq_len=N,
+                        parallelism=f"(b,kv-group) units, dp{world}, no collective",
                         l2="inputs larger than L2 (Q, dO 512 MiB each); no flush"),
             fwd=dict(value=round(world * flops_fwd / (ms_fwd * 1e-3) / 1e12, 2), unit="TFLOPS/s",
                      ms=round(ms_fwd, 3)),
             roofline=roofline, cpu_baseline=cpu, e2e=e2e, clocks=clocks.summary(),
             gpu_launches=(1 + len(names)) * args.steps, kernel_status=status,
             bwd_path="materialised (workspace %d bytes)" % ws_bytes if len(names) == 2 else "recompute",
+            peak_mem_gb=round(peak_gb, 3), recompute_bwd=recompute, sweep=sweep, cfg4_1gpu=cfg4,
+        )
+        print(json.dumps(line), flush=True)
+
+
+def run_cfg4_one_gpu(device, stream, steps=3, warmup=2):
+    """Config 4 on one GPU through the same UnitShardedAttention step the
+    multi-GPU line runs (no collective at world size 1): the strong-scaling
+    reference."""
+    from gemma_triton_flash_attn.flops import attn_flops
+    from gemma_triton_flash_attn.sharding import UnitShardedAttention
+
+    wl = WORKLOADS["cfg4"]
+    B, Hq, Hkv, N, D = wl["B"], wl["Hq"], wl["Hkv"], wl["N"], wl["D"]
+    q, k, v, do = make_inputs(wl, 1234, device)
+    att = UnitShardedAttention(B, Hq, Hkv, N, D, wl["dtype"], device, causal=True)
+    for _ in range(warmup):
+        att.step(q, k, v, do)
+    torch.cuda.synchronize()
+    ms = time_loop(lambda: att.step(q, k, v, do), steps, stream)
+    res = dict(value=round(attn_flops(B, Hq, N, D, True, 0, bwd=True) / (ms * 1e-3) / 1e12, 2), unit="TFLOPS/s",
+               ms_per_step=round(ms, 3), workload=wl["name"])
+    del att, q, k, v, do
+    torch.cuda.empty_cache()
+    return res
+
+
+# ------------------------------------------------------------------ N GPUs, one problem
+def run_strong(args, wl, world, rank, local):
+    """Strong scaling: one config-4 problem over all ranks in (batch, KV-head)
+    unit blocks; O, LSE, dQ, dK, dV all-gathered on every rank inside the step."""
+    from gemma_triton_flash_attn import _lib
+    from gemma_triton_flash_attn.flops import attn_flops, kernel_flops
+    from gemma_triton_flash_attn.sharding import UnitShardedAttention
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(device)
+    B, Hq, Hkv, N, D, causal = (wl[x] for x in ("B", "Hq", "Hkv", "N", "D", "causal"))
+    window = _window(wl)
+    q, k, v, do = make_inputs(wl, 1234, device)  # the same problem on every rank
+    att = UnitShardedAttention(B, Hq, Hkv, N, D, wl["dtype"], device, causal=causal, slide_size=wl["W"])
+    step = lambda: att.step(q, k, v, do)  # noqa: E731
+    total = attn_flops(B, Hq, N, D, causal, window, bwd=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    with ClockSampler(_uuid(device)) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = time_loop(step, args.steps, stream)
+        barrier(world)
+    ms_max = max_over_ranks(ms, world, device)
+    value = total / (ms_max * 1e-3) / 1e12
+
+    # the same kernels with the collectives left out: the exposed share of the
+    # all-gathers is the difference
+    def compute_only():
+        w = att.world
+        att.world = 1
+        try:
+            att.forward(q, k, v)
+            att.backward(q, k, v, do)
+        finally:
+            att.world = w
+
+    compute_only()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_c = max_over_ranks(time_loop(compute_only, args.steps, stream), world, device)
+    status = _lib.device_status(local)
+    gathered = sum(t.numel() * t.element_size() for t in (att.o, att.lse, att.dq, att.dk, att.dv))
+
+    # end to end: each rank uploads its own units' q, k, v, dO from pinned host
+    # memory and downloads its own units' dQ, dK, dV; the all-gathers still
+    # reassemble every output on every rank inside the step.
+    e2e = None
+    if not args.no_e2e:
+        hq_, hk_ = [], []
+        for i in range(len(att.runs)):
+            hq_.append([att._qv(i, t).cpu().pin_memory() for t in (q, do)])
+            hk_.append([att._kvv(i, t).cpu().pin_memory() for t in (k, v)])
+        outs = [[torch.empty(att._qv(i, att.dq).shape, dtype=q.dtype).pin_memory(),
+                 torch.empty(att._kvv(i, att.dk).shape, dtype=k.dtype).pin_memory(),
+                 torch.empty(att._kvv(i, att.dv).shape, dtype=v.dtype).pin_memory()] for i in range(len(att.runs))]
+        down = torch.cuda.Stream(device)
+
+        def e2e_step():
+            for i in range(len(att.runs)):
+                att._qv(i, q).copy_(hq_[i][0], non_blocking=True)
+                att._qv(i, do).copy_(hq_[i][1], non_blocking=True)
+                att._kvv(i, k).copy_(hk_[i][0], non_blocking=True)
+                att._kvv(i, v).copy_(hk_[i][1], non_blocking=True)
+            step()
+            down.wait_stream(stream)
+            with torch.cuda.stream(down):
+                for i in range(len(att.runs)):
+                    outs[i][0].copy_(att._qv(i, att.dq), non_blocking=True)
+                    outs[i][1].copy_(att._kvv(i, att.dk), non_blocking=True)
+                    outs[i][2].copy_(att._kvv(i, att.dv), non_blocking=True)
+            stream.wait_stream(down)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        ms_e = max_over_ranks(time_loop(e2e_step, args.steps, stream), world, device)
+        h2d = sum(t.numel() * t.element_size() for r in hq_ + hk_ for t in r)
+        d2h = sum(t.numel() * t.element_size() for r in outs for t in r)
+        e2e = dict(value=round(total / (ms_e * 1e-3) / 1e12, 2), unit="TFLOPS/s", ms_per_step=round(ms_e, 3),
+                   h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
+                   pipeline="each rank copies only its own units in and out; all-gathers inside the step")
+
+    peaks = measured_peaks()
+    per_rank = total / world
+    if rank == 0:
+        line = dict(
+            metric=METRIC, value=round(value, 2), unit="TFLOPS/s", n_gpus=world, steps=args.steps,
+            warmup=args.warmup, ms_per_step=round(ms_max, 3), higher_is_better=True, scaling="strong",
+            vs_baseline=None, dtype="bf16" if wl["dtype"] == torch.bfloat16 else "fp16",
+            data="synthetic (seeded N(0,1)*%g, the same problem on every rank)" % wl["factor"],
+            config=dict(workload=wl["name"], global_batch=B, H_Q=Hq, H_KV=Hkv, N=N, D=D, causal=causal,
+                        seq_len=N, units=B * Hkv, units_per_gpu=B * Hkv // world,
+                        parallelism=f"{B * Hkv} (b,kv-group) units in equal blocks over {world} GPUs; "
+                                    "O/LSE/dQ/dK/dV all-gathered (NCCL) inside the step",
+                        l2="inputs larger than L2 (Q, dO 1 GiB each); no flush"),
+            collective=dict(ms_compute_only=round(ms_c, 3), exposed_ms=round(ms_max - ms_c, 3),
+                            exposed_share=round(max(0.0, ms_max - ms_c) / ms_max, 4),
+                            bytes_gathered_per_rank=round(gathered * (world - 1) / world),
+                            op="all_gather_into_tensor x5 (in place), overlapped with the next kernels"),
+            roofline=dict(bound="tensor", kernel="whole step per rank", achieved=round(per_rank / ms_max / 1e9, 1),
+                          peak=peaks["tflops_burst"], unit="TFLOP/s",
+                          frac=round(per_rank / ms_max / 1e9 / peaks["tflops_burst"], 4), traffic=None),
+            e2e=e2e, clocks=clocks.summary(), kernel_status=status,
+            gpu_launches=3 * len(att.runs) * args.steps,
+            gpu_launches_note="per rank and step: per run of units 1 forward, 1 dQ+P/dS, 1 dK+dV kernel "
+                              "(plus 5 NCCL all-gathers, not counted)",
         )
         print(json.dumps(line), flush=True)
 
@@ -504,8 +751,7 @@ def run_decoder(args, wl, world, rank, local):
         step()
     torch.cuda.synchronize()
     barrier(world)
-    uuid = str(torch.cuda.get_device_properties(device).uuid)
-    with ClockSampler([uuid if uuid.startswith("GPU-") else "GPU-" + uuid]) as clocks:
+    with ClockSampler(_uuid(device)) as clocks:
         ms = max_over_ranks(time_loop(step, args.steps, stream), world, device)
     n_glob = sum(cfg.is_global(i) for i in range(cfg.num_layers))
     attn_fl = n_glob * attn_flops(1, cfg.global_heads, N, cfg.global_head_dim, True) + \
@@ -515,99 +761,71 @@ def run_decoder(args, wl, world, rank, local):
                     value=round(world * N / (ms * 1e-3), 1), unit="tokens/s", n_gpus=world, steps=args.steps,
                     warmup=args.warmup, ms_per_step=round(ms, 3), higher_is_better=True, scaling="weak",
                     vs_baseline=None, dtype="bf16", data="synthetic (seeded uniform token ids, random-init weights)",
-                    config=dict(workload=wl["name"], global_batch=world, seq_len=N, parallelism=f"one sequence per GPU, dp{world}"),
+                    config=dict(workload=wl["name"], global_batch=world, seq_len=N,
+                                parallelism=f"one sequence per GPU, dp{world}"),
                     attention_tflops_in_step=round(attn_fl / (ms * 1e-3) / 1e12, 1),
-                    e2e=dict(value=round(world * N / (ms * 1e-3), 1), unit="tokens/s", h2d_bytes_per_step=ids_h.numel() * 8,
-                             d2h_bytes_per_step=8),
+                    e2e=dict(value=round(world * N / (ms * 1e-3), 1), unit="tokens/s",
+                             h2d_bytes_per_step=ids_h.numel() * 8, d2h_bytes_per_step=8),
                     clocks=clocks.summary(), gpu_launches=35 * args.steps)
         print(json.dumps(line), flush=True)
 
 
-def run_strong(args, wl, world, rank, local):
-    """Strong scaling: the whole job is one problem; every rank ends with the
-    complete O, LSE, dQ, dK, dV (the all-gathers are inside the timed step)."""
-    from gemma_triton_flash_attn.flops import attn_flops
-    from gemma_triton_flash_attn.sharding import (head_split_backward, head_split_forward, sharded_backward,
-                                                  sharded_forward)
-
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    stream = torch.cuda.current_stream(device)
-    B, Hq, Hkv, N, D, causal, W = (wl[x] for x in ("B", "Hq", "Hkv", "N", "D", "causal", "W"))
-    q, k, v, do = make_inputs(wl, 1234, device)  # same problem on every rank
-    split = world > B * Hkv
-    fwd, bwd = (head_split_forward, head_split_backward) if split else (sharded_forward, sharded_backward)
-
-    def step():
-        o, lse = fwd(q, k, v, causal, W)
-        bwd(q, k, v, o, lse, do, causal, W)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    uuid = str(torch.cuda.get_device_properties(device).uuid)
-    with ClockSampler([uuid if uuid.startswith("GPU-") else "GPU-" + uuid]) as clocks:
-        ms = max_over_ranks(time_loop(step, args.steps, stream), world, device)
-    window = W if (causal and 0 < W < N) else 0
-    total = attn_flops(B, Hq, N, D, causal, window, bwd=True)
-    if rank == 0:
-        line = dict(metric=METRIC + " (strong scaling)", value=round(total / (ms * 1e-3) / 1e12, 2), unit="TFLOPS/s",
-                    n_gpus=world, steps=args.steps, warmup=args.warmup, ms_per_step=round(ms, 3),
-                    higher_is_better=True, scaling="strong", vs_baseline=None,
-                    dtype="bf16" if wl["dtype"] == torch.bfloat16 else "fp16", data="synthetic",
-                    config=dict(workload=wl["name"], global_batch=B, seq_len=N,
-                                parallelism=("query heads of each (b, kv-group) unit split, dK/dV all-reduced"
-                                             if split else "(b, kv-group) units")
-                                + f" over {world} GPUs, outputs all-gathered"),
-                    clocks=clocks.summary(), gpu_launches=4 * args.steps)
-        print(json.dumps(line), flush=True)
-
-
+# ------------------------------------------------------------------ reference arm
 def run_reference(args, wl, world, rank):
+    """The reference's eager CPU path (oracle/eager_ref.py) on the host cores:
+    each step is one fp32 fwd+bwd of the bounded sample of `wl` that
+    cpu_eager_sample describes. Rank 0 only; other ranks exit without work."""
     if rank != 0:
         return
-    cores = os.cpu_count()
-    rows = cpu_calibrate(wl, args.cpu_seconds)
-    for s in range(args.warmup):
-        cpu_sample_run(wl, max(64, rows // 8), seed=100 + s)
-    times, fl = [], None
-    for s in range(args.steps):
-        dt, fl = cpu_sample_run(wl, rows, seed=s)
-        times.append(dt)
-    t = statistics.mean(times)
-    value = fl / t / 1e12
-    sample = (f"oracle port (numpy fp32, {cores} BLAS threads): fwd+bwd of query head 0, the last {rows} "
-              f"query rows of N={wl['N']} (D={wl['D']}) against all keys per step")
+    from gemma_triton_flash_attn.flops import attn_flops
+    from oracle.eager_ref import time_fwd_bwd, use_all_cores
+
+    threads = use_all_cores()
+    N, D, causal = wl["N"], wl["D"], wl["causal"]
+    window = _window(wl)
+    hq = min(CPU_SAMPLE_HEADS, wl["Hq"] // wl["Hkv"])
+    g = torch.Generator().manual_seed(0)
+    mk = lambda *s: (torch.randn(*s, generator=g) * wl["factor"]).to(wl["dtype"]).float()  # noqa: E731
+    q, k, v, do = mk(1, hq, N, D), mk(1, 1, N, D), mk(1, 1, N, D), mk(1, hq, N, D)
+    t = time_fwd_bwd(q, k, v, do, causal, window, warmup=args.warmup, reps=args.steps)
+    value = attn_flops(1, hq, N, D, causal, window, bwd=True) / t / 1e12
+    sample = (f"reference eager path (KV heads repeated + torch SDPA, fp32, autograd backward; oracle/eager_ref.py) "
+              f"on {threads} threads: fwd+bwd of query heads 0-{hq - 1} of KV group 0 at N={N}, D={D} per step")
     line = dict(
         metric=METRIC, value=round(value, 5), unit="TFLOPS/s", n_gpus=world, steps=args.steps,
-        warmup=args.warmup, ms_per_step=round(t * 1e3, 1), higher_is_better=True, scaling="weak",
+        warmup=args.warmup, ms_per_step=round(t * 1e3, 1), higher_is_better=True,
+        scaling="strong" if args.workload == "cfg4" else "weak",
         vs_baseline=None, dtype="f32", data="synthetic", impl="reference",
-        config=dict(workload=wl["name"], B_per_gpu=wl["B"], H_Q=wl["Hq"], H_KV=wl["Hkv"], N=wl["N"], D=wl["D"],
-                    causal=wl["causal"], window=wl["W"], global_batch=wl["B"] * world, seq_len=wl["N"],
-                    parallelism="host cores"),
-        cpu_baseline=dict(value=round(value, 5), unit="TFLOPS/s", cores=cores, kind="port", sample=sample),
+        config=dict(workload=wl["name"], B=wl["B"], H_Q=wl["Hq"], H_KV=wl["Hkv"], N=N, D=D, causal=causal,
+                    window=window, global_batch=wl["B"], seq_len=N, parallelism="host cores"),
+        cpu_baseline=dict(value=round(value, 5), unit="TFLOPS/s", cores=threads, kind="port", sample=sample),
         e2e=dict(value=round(value, 5), unit="TFLOPS/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+        config1=cpu_config1(),
     )
     print(json.dumps(line), flush=True)
 
 
 def main():
     args = parse_args()
-    wl = dict(WORKLOADS[args.workload])
+    world, rank, local = setup_dist()
+    if args.workload is None:
+        args.workload = "cfg4" if (world > 1 and args.scaling == "strong") else "cfg2"
+    wl = WORKLOADS[args.workload]
     if args.seqlen:
+        wl = dict(wl)
         wl["N"] = args.seqlen
         wl["name"] = wl["name"].replace("N=16384", f"N={args.seqlen}")
-    world, rank, local = setup_dist()
     try:
         if args.impl == "reference":
             run_reference(args, wl, world, rank)
+        elif args.only:
+            run_only(args, wl, local)
         elif args.workload == "cfg5":
             run_decoder(args, wl, world, rank, local)
-        elif args.strong:
+        elif args.workload == "cfg4":
             run_strong(args, wl, world, rank, local)
         else:
-            run_ours(args, wl, world, rank, local)
+            run_single(args, wl, world, rank, local)
     finally:
         if world > 1 and dist.is_initialized():
             dist.destroy_process_group()

@@ -199,12 +199,25 @@ def _fwd(q, k, v, causal, window, scale, want_lse, rows=None, out=None):
     return o, lse
 
 
-def _workspace_limit():
-    """Largest backward workspace (bytes) `_bwd` may allocate; GQAFA_BWD_WORKSPACE_LIMIT
-    overrides (0 turns the materialised backward off). Default: no limit beyond
-    what the allocator can give."""
+def _workspace_limit(device=None):
+    """Largest backward workspace (bytes) `_bwd` may allocate.
+
+    GQAFA_BWD_WORKSPACE_LIMIT (bytes) overrides; 0 turns the materialised
+    backward off. Otherwise the budget is GQAFA_BWD_WORKSPACE_FRACTION
+    (default 0.5) of the device memory that is free right now: free in the
+    driver plus what torch's caching allocator holds unused. A workspace over
+    the budget makes the backward run over groups of KV heads (each group's
+    share within the budget), and the recomputing backward (no workspace) when
+    one KV head's share is over it too."""
     env = os.environ.get("GQAFA_BWD_WORKSPACE_LIMIT")
-    return None if env is None else int(env)
+    if env is not None:
+        return int(env)
+    if device is None:
+        return None
+    frac = float(os.environ.get("GQAFA_BWD_WORKSPACE_FRACTION", "0.5"))
+    free, _ = torch.cuda.mem_get_info(device)
+    cached = torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)
+    return int(frac * (free + cached))
 
 
 def bwd_workspace_size(b, h_q, h_kv, n, d, causal, window):
@@ -216,7 +229,7 @@ def bwd_workspace_size(b, h_q, h_kv, n, d, causal, window):
 
 
 def _alloc_workspace(size, device):
-    limit = _workspace_limit()
+    limit = _workspace_limit(device)
     if size <= 0 or (limit is not None and size > limit):
         return None
     try:
@@ -235,7 +248,7 @@ def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=
     path (gqafa_bwd_ws: the dQ kernel stores P and dS, one kernel makes dK and
     dV from them) with a workspace from the caching allocator, or `workspace`
     when given; when the whole workspace does not fit (memory or
-    GQAFA_BWD_WORKSPACE_LIMIT) it runs over groups of KV heads, and without
+    the budget of _workspace_limit) it runs over groups of KV heads, and without
     room for one KV head's share it runs the recomputing gqafa_bwd. With a
     `workspace` tensor, `stage` 0 / 1 selects that path's kernels instead."""
     lib = _lib.load()
@@ -250,6 +263,11 @@ def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=
         delta = torch.empty((b, h_q, n), dtype=torch.float32, device=q.device)
     else:
         dq, dk, dv, delta = out
+    # the C ABI reads LSE and delta as contiguous [B, H_Q, N] fp32 arrays
+    if not lse.is_contiguous():
+        lse = lse.contiguous()
+    if not delta.is_contiguous():
+        raise ValueError("delta must be a contiguous (B, H_Q, N) float32 tensor")
     ws = workspace
     chunks = None
     if ws is None and stage is None and rows is None:
@@ -291,8 +309,7 @@ def _workspace_chunks(size, b, h_kv, device):
     one KV head's share does not fit either (the caller then recomputes). The
     workspace is linear in B * H_Q, so one KV head of one batch element needs
     size / (B * H_KV)."""
-    limit = _workspace_limit()
-    if limit == 0:
+    if _workspace_limit() == 0:
         return None, None
     per_head = size // (b * h_kv)
     hc = h_kv if b > 1 else h_kv // 2

@@ -24,8 +24,8 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-__all__ = ["ShardPlan", "sharded_forward", "sharded_backward", "SequenceSplitPlan", "balanced_row_ranges",
-           "split_forward", "split_backward", "head_split_assignment", "head_split_forward",
+__all__ = ["ShardPlan", "sharded_forward", "sharded_backward", "UnitShardedAttention", "SequenceSplitPlan",
+           "balanced_row_ranges", "split_forward", "split_backward", "head_split_assignment", "head_split_forward",
            "head_split_backward"]
 
 
@@ -151,6 +151,153 @@ def sharded_backward(q, k, v, o, lse, do, causal=False, slide_size=0, softmax_sc
         dk_loc = _gather_units(plan, dk_loc, group)
         dv_loc = _gather_units(plan, dv_loc, group)
     return (dq_loc.reshape(B, Hq, N, D), dk_loc.reshape(B, Hkv, N, D), dv_loc.reshape(B, Hkv, N, D))
+
+
+# --------------------------------------------------------------------------
+# Persistent-buffer unit sharding with overlapped all-gathers
+# --------------------------------------------------------------------------
+
+
+class UnitShardedAttention:
+    """Forward + backward of one attention problem over the ranks of `group`,
+    each rank computing whole (batch, KV-head) units, with the outputs
+    reassembled on every rank by all-gathers that run while the next kernels
+    compute.
+
+    The output tensors (O, LSE, dQ, dK, dV, delta) are allocated once, full
+    size and contiguous. Units are numbered u = b * H_KV + kv_head, so the
+    query heads of a block of consecutive units are one contiguous range of the
+    flattened (B * H_Q, N, D) storage: every rank's kernels write straight
+    into its own slice and an in-place ``all_gather_into_tensor`` fills the
+    other ranks' slices. No copies are made on either side.
+
+    Order of work on the calling stream, with the collectives on the process
+    group's own stream:
+
+        forward kernels -> all-gather O, LSE      (overlaps the backward kernels)
+        dQ + P/dS kernels -> all-gather dQ        (overlaps the dK/dV kernels)
+        dK/dV kernels -> all-gather dK, dV
+        ``wait()``: the calling stream waits for the four collectives
+
+    Requires B * H_KV to be a multiple of the world size (equal blocks, which
+    the in-place all-gather needs); ``sharded_forward`` / ``sharded_backward``
+    handle the uneven case. The per-unit kernels are the materialised backward
+    (``gqafa_bwd_ws``) with one workspace per contiguous run of units, so the
+    dQ stage of every run can precede all dK/dV stages.
+
+    ``fwd_fn(q, k, v, o, lse)`` and ``bwd_fn(stage, q, k, v, o, lse, do, dq,
+    dk, dv, delta, workspace)`` replace the kernels (CPU tests); by default
+    they are this library's CUDA launches.
+    """
+
+    def __init__(self, batch, heads_q, heads_kv, seqlen, head_dim, dtype, device, causal=True, slide_size=0,
+                 softmax_scale=None, group=None, fwd_fn=None, bwd_fn=None):
+        from .attention import _normalize_window
+
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.plan = ShardPlan(batch, heads_q, heads_kv, self.world, self.rank)
+        if self.plan.num_units % self.world != 0:
+            raise ValueError(f"{self.plan.num_units} (batch, KV-head) units do not divide over {self.world} ranks")
+        self.shape = (batch, heads_q, heads_kv, seqlen, head_dim)
+        self.causal = bool(causal)
+        self.window = _normalize_window(causal, slide_size, seqlen)
+        self.scale = (1.0 / math.sqrt(head_dim)) if softmax_scale is None else float(softmax_scale)
+        B, Hq, Hkv, N, D = self.shape
+        kw = dict(dtype=dtype, device=device)
+        self.o = torch.empty((B, Hq, N, D), **kw)
+        self.dq = torch.empty((B, Hq, N, D), **kw)
+        self.dk = torch.empty((B, Hkv, N, D), **kw)
+        self.dv = torch.empty((B, Hkv, N, D), **kw)
+        self.lse = torch.empty((B, Hq, N), dtype=torch.float32, device=device)
+        self.delta = torch.empty((B, Hq, N), dtype=torch.float32, device=device)
+        self.runs = list(self.plan.runs())
+        self._fwd_fn = fwd_fn or self._kernel_fwd
+        self._bwd_fn = bwd_fn or self._kernel_bwd
+        self.workspaces = None
+        if bwd_fn is None:
+            from .attention import _alloc_workspace, bwd_workspace_size
+
+            G = Hq // Hkv
+            self.workspaces = []
+            for _, kv0, kv1 in self.runs:
+                size = bwd_workspace_size(1, (kv1 - kv0) * G, kv1 - kv0, N, D, self.causal, self.window)
+                ws = _alloc_workspace(size, device)
+                if ws is None and size > 0:
+                    raise MemoryError(f"no room for the {size}-byte backward workspace of a run of units")
+                self.workspaces.append(ws)
+        self._works = []
+
+    # ---- kernels -------------------------------------------------------------
+    def _kernel_fwd(self, q, k, v, o, lse):
+        from .attention import _fwd
+
+        _fwd(q, k, v, self.causal, self.window, self.scale, True, out=(o, lse))
+
+    def _kernel_bwd(self, stage, q, k, v, o, lse, do, dq, dk, dv, delta, workspace):
+        from .attention import _bwd
+
+        _bwd(q, k, v, o, lse, do, self.causal, self.window, self.scale, stage=stage, out=(dq, dk, dv, delta),
+             workspace=workspace)
+
+    # ---- slices --------------------------------------------------------------
+    def _qv(self, i, t):
+        """Run i's query heads of a [B, H_Q, ...] tensor (a view)."""
+        b, kv0, kv1 = self.runs[i]
+        G = self.plan.group
+        return t[b:b + 1, kv0 * G:kv1 * G]
+
+    def _kvv(self, i, t):
+        """Run i's KV heads of a [B, H_KV, ...] tensor (a view)."""
+        b, kv0, kv1 = self.runs[i]
+        return t[b:b + 1, kv0:kv1]
+
+    def _gather(self, t):
+        """Start the in-place all-gather of this rank's block of `t` (flattened
+        over batch and heads, which are unit-ordered)."""
+        if self.world == 1:
+            return
+        flat = t.view(self.world, -1)
+        self._works.append(dist.all_gather_into_tensor(t.view(-1), flat[self.rank], group=self.group, async_op=True))
+
+    # ---- passes --------------------------------------------------------------
+    def forward(self, q, k, v):
+        """O and LSE of this rank's units, then their all-gather (started, not awaited)."""
+        for i in range(len(self.runs)):
+            self._fwd_fn(self._qv(i, q), self._kvv(i, k), self._kvv(i, v), self._qv(i, self.o), self._qv(i, self.lse))
+        self._gather(self.o)
+        self._gather(self.lse)
+        return self.o, self.lse
+
+    def backward(self, q, k, v, do):
+        """dQ, dK, dV of this rank's units (from this rank's own O / LSE rows,
+        which the all-gather does not touch), each followed by its all-gather."""
+        n = len(self.runs)
+        for stage in (0, 1):
+            for i in range(n):
+                qv, kvv = (lambda t: self._qv(i, t)), (lambda t: self._kvv(i, t))
+                ws = self.workspaces[i] if self.workspaces is not None else None
+                self._bwd_fn(stage, qv(q), kvv(k), kvv(v), qv(self.o), qv(self.lse), qv(do), qv(self.dq),
+                             kvv(self.dk), kvv(self.dv), qv(self.delta), ws)
+            if stage == 0:
+                self._gather(self.dq)
+        self._gather(self.dk)
+        self._gather(self.dv)
+        return self.dq, self.dk, self.dv
+
+    def wait(self):
+        """Make the calling stream wait for every collective started so far."""
+        for w in self._works:
+            w.wait()
+        self._works = []
+
+    def step(self, q, k, v, do):
+        """One full forward + backward with every output reassembled on every rank."""
+        self.forward(q, k, v)
+        self.backward(q, k, v, do)
+        self.wait()
+        return self.o, self.lse, self.dq, self.dk, self.dv
 
 
 # --------------------------------------------------------------------------

@@ -1,5 +1,7 @@
 """The CPU oracle, pinned against fixtures produced by the reference's own
 eager attention (tests/golden/make_golden.py). CPU only."""
+import os
+
 import numpy as np
 import pytest
 
@@ -49,3 +51,61 @@ def test_flop_conventions():
     assert attended_pairs(4096, True, 1024) == 4096 * 1024 - 1024 * 1023 // 2
     assert attended_pairs(512, True, 1024) == 512 * 512 // 2
     assert attended_pairs(100, False, 7) == 100 * 100
+
+
+# ---------------------------------------------------------------- eager CPU path
+# oracle/eager_ref.py restates the reference's eager attention_gqa_ref /
+# attention_swa_ref (flash_attn/attention.py:611-642): the CPU path that
+# bench.py times as the reference arm. It is pinned to the same fixtures and,
+# where a checkout of the reference is present, to the reference module itself.
+REF_ROOT = os.environ.get("GQAFA_REFERENCE_ROOT", "/root/reference")
+
+
+def _eager_run(c):
+    import torch
+
+    from oracle.eager_ref import sdpa_gqa
+
+    q, k, v = (c[x].float().requires_grad_(True) for x in ("q", "k", "v"))
+    o = sdpa_gqa(q, k, v, c["causal"], c["slide"])
+    o.backward(c["do"].float())
+    return o.detach(), q.grad, k.grad, v.grad
+
+
+@pytest.mark.parametrize("path", golden_cases(), ids=lambda p: p.split("/")[-1][:-4])
+def test_eager_restatement_matches_reference_fixtures(path):
+    c = load_golden(path)
+    o, dq, dk, dv = _eager_run(c)
+    for name, x in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv)):
+        ref = c[name]
+        err = (x - ref).abs().max().item() / max(1.0, ref.abs().max().item())
+        assert err < 1e-5, f"{name}: rel err {err}"
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF_ROOT, "flash_attn")), reason="no reference checkout")
+@pytest.mark.parametrize("causal", [True, False])
+def test_eager_restatement_is_the_reference_function(causal):
+    """Config-1-shaped (smaller N) fp32 inputs: bitwise equal to the reference's
+    own attention_gqa_ref, forward and autograd backward."""
+    import importlib.util
+
+    import torch
+
+    from oracle.eager_ref import sdpa_gqa
+
+    spec = importlib.util.spec_from_file_location("_ref_attention", os.path.join(REF_ROOT, "flash_attn", "attention.py"))
+    try:
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    except Exception as e:  # the module imports triton at top level
+        pytest.skip(f"reference module not importable here: {e}")
+    g = torch.Generator().manual_seed(7)
+    q, k, v, do = (torch.randn(s, generator=g) for s in ((1, 8, 64, 32), (1, 2, 64, 32), (1, 2, 64, 32), (1, 8, 64, 32)))
+    outs = []
+    for fn in (mod.attention_gqa_ref, lambda a, b, c_, causal: sdpa_gqa(a, b, c_, causal)):
+        qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
+        o = fn(qq, kk, vv, causal=causal)
+        o.backward(do)
+        outs.append((o.detach(), qq.grad, kk.grad, vv.grad))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)

@@ -143,3 +143,73 @@ def test_head_split_assignment():
     assert got == [(0, kv, kv * 8 + p * 4, 4) for kv in range(4) for p in range(2)]
     with pytest.raises(ValueError):
         head_split_assignment(1, 12, 4, 8, 0)  # 3 heads per group, 2 ranks per unit
+
+
+# ---------------------------------------------------------------- persistent-buffer unit sharding
+def _unit_worker(rank, world, port, out_dir):
+    from gemma_triton_flash_attn.sharding import UnitShardedAttention
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        q, k, v, do = _inputs()
+        B, Hq, N, D = q.shape
+        calls = []
+
+        def fwd_fn(qs, ks, vs, o, lse):
+            calls.append(("fwd", qs.shape[1]))
+            oo, ll = oracle_fwd(qs, ks, vs, True, 5, None)
+            o.copy_(oo)
+            lse.copy_(ll)
+
+        def bwd_fn(stage, qs, ks, vs, o, lse, dos, dq, dk, dv, delta, ws):
+            # the stand-in reads only this rank's own O / LSE rows, as the kernels do
+            calls.append((f"bwd{stage}", qs.shape[1]))
+            gq, gk, gv = oracle_bwd(qs, ks, vs, o.clone(), lse.clone(), dos, True, 5, None)
+            if stage == 0:
+                dq.copy_(gq)
+                delta.copy_((dos * o).sum(-1))
+            else:
+                dk.copy_(gk)
+                dv.copy_(gv)
+
+        att = UnitShardedAttention(B, Hq, k.shape[1], N, D, q.dtype, q.device, causal=True, slide_size=5,
+                                   fwd_fn=fwd_fn, bwd_fn=bwd_fn)
+        o, lse, dq, dk, dv = att.step(q, k, v, do)
+        # a second step reuses the buffers
+        o, lse, dq, dk, dv = att.step(q, k, v, do)
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), o=o.numpy(), lse=lse.numpy(), dq=dq.numpy(),
+                 dk=dk.numpy(), dv=dv.numpy(), runs=np.array(att.runs))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3, 6])
+def test_unit_sharded_attention_matches_single_rank(tmp_path, world):
+    port = _free_port()
+    mp.spawn(_unit_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+    q, k, v, do = _inputs()
+    o, lse = oracle_fwd(q, k, v, True, 5, None)
+    dq, dk, dv = oracle_bwd(q, k, v, o, lse, do, True, 5, None)
+    units = []
+    for r in range(world):
+        z = np.load(os.path.join(tmp_path, f"r{r}.npz"))
+        units += [int(b) * 3 + kv for b, kv0, kv1 in z["runs"] for kv in range(kv0, kv1)]
+        for name, ref in (("o", o), ("lse", lse), ("dq", dq), ("dk", dk), ("dv", dv)):
+            np.testing.assert_allclose(z[name], ref.numpy(), rtol=1e-5, atol=1e-5, err_msg=f"rank {r} {name}")
+    assert units == list(range(6))  # every (b, kv) unit computed by exactly one rank
+
+
+def test_unit_sharded_attention_single_rank_runs():
+    from gemma_triton_flash_attn.sharding import ShardPlan, UnitShardedAttention
+
+    assert ShardPlan(2, 6, 3, 4, 0).num_units % 4 != 0
+    port = _free_port()
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        # one rank owns all six units: one run per batch element
+        att = UnitShardedAttention(2, 6, 3, 33, 16, torch.float32, "cpu", fwd_fn=lambda *a: None,
+                                   bwd_fn=lambda *a: None)
+        assert att.runs == [(0, 0, 3), (1, 0, 3)]
+    finally:
+        dist.destroy_process_group()
