@@ -36,7 +36,16 @@ def _worker(rank, world, port, out_dir, split=False):
     try:
         from gemma_triton_flash_attn import sharding as sh
 
-        q, k, v, do = _inputs(f"cuda:{rank}", split)
+        q, k, v, do = _inputs(f"cuda:{rank}", split in ("seq", "heads"))
+        if split == "persistent":
+            att = sh.UnitShardedAttention(q.shape[0], q.shape[1], k.shape[1], q.shape[2], q.shape[3], q.dtype,
+                                          q.device, causal=True)
+            for _ in range(2):  # the second step reuses every buffer
+                o, lse, dq, dk, dv = att.step(q, k, v, do)
+            torch.cuda.synchronize()
+            torch.save({n: t.cpu() for n, t in dict(o=o, lse=lse, dq=dq, dk=dk, dv=dv).items()},
+                       os.path.join(out_dir, f"r{rank}.pt"))
+            return
         fwd, bwd = {False: (sh.sharded_forward, sh.sharded_backward), "seq": (sh.split_forward, sh.split_backward),
                     "heads": (sh.head_split_forward, sh.head_split_backward)}[split]
         o, lse = fwd(q, k, v, True, 0)
@@ -47,17 +56,18 @@ def _worker(rank, world, port, out_dir, split=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("split", [False, "seq", "heads"], ids=["units", "sequence_split", "head_split"])
+@pytest.mark.parametrize("split", [False, "persistent", "seq", "heads"],
+                         ids=["units", "unit_sharded_attention", "sequence_split", "head_split"])
 def test_sharded_equals_single_gpu(tmp_path, split):
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs at least two GPUs")
-    if split:
+    if split in ("seq", "heads"):
         world = 2  # one (batch, KV-group) unit split over two ranks by sequence blocks
     from gemma_triton_flash_attn.attention import flash_attn_gqa_backward, flash_attn_gqa_forward_with_lse
 
     mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), split), nprocs=world, join=True)
-    q, k, v, do = _inputs("cuda:0", split)
+    q, k, v, do = _inputs("cuda:0", split in ("seq", "heads"))
     o, lse = flash_attn_gqa_forward_with_lse(q, k, v, True, 0)
     dq, dk, dv = flash_attn_gqa_backward(q, k, v, o, lse, do, True, 0)
     ref = dict(o=o, lse=lse, dq=dq, dk=dk, dv=dv)
