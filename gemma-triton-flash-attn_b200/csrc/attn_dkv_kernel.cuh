@@ -122,13 +122,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
 
   if (warp == 0) {
     // ======================= TMA producer (both CTAs) =======================
-    if (lane == 0) {
+    if (lane == 0 && !p.no_loads) {
       bool ok = true;
       uint32_t cnt = 0;
       auto acquire = [&](int& st) -> bool {
         st = cnt % NST;
         const uint32_t ph = (cnt / NST) & 1u;
-        if (!mbar_wait_cluster(BAR_EMPTY(st), ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_RING_EMPTY)) return false;
+        if (!mbar_wait_cluster(BAR_EMPTY(st), ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_RING_EMPTY, p.wait_limit)) return false;
         if (leader) mbar_arrive_expect_tx(BAR_FULL(st), 2 * C::STAGE_BYTES);
         ++cnt;
         return true;
@@ -178,7 +178,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       bool first = true;
       const uint64_t dRing = sw128_desc(smem_u32(sRing), C::PANEL_BYTES, 1024);
       auto full = [&](uint32_t c) {
-        return mbar_wait_cluster(BAR_FULL(c % NST), (c / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL);
+        return mbar_wait_cluster(BAR_FULL(c % NST), (c / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL, p.wait_limit);
       };
       auto sdesc = [&](uint32_t c) { return dRing + static_cast<uint64_t>(((c % NST) * C::STAGE_BYTES) >> 4); };
       for (int g0 = 0; g0 < G && ok; ++g0) {
@@ -226,7 +226,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     for (int t = t_lo; t < t_hi && !any; ++t) any = stored(t);
     bool ok = true;
     if (any) {
-      ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
+      ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC, p.wait_limit);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) tc_fence_after();
     }

@@ -72,6 +72,11 @@ struct KParams {
   // Optional diagnostics: when non-null, each CTA adds the cycles its roles
   // spend waiting (see WaitCounter) into these counters. Null on the hot path.
   unsigned long long* prof;
+  // Bound of every mbarrier wait, in clock cycles (WAIT_LIMIT_CYCLES unless a
+  // test set a short one), and a test switch that makes the TMA producer
+  // issue nothing, so every wait of the launch runs into that bound.
+  long long wait_limit;
+  int no_loads;
 };
 
 // Indices of the wait-cycle diagnostics counters.
@@ -297,7 +302,7 @@ __global__ void __launch_bounds__(256, 1)
 
   if (warp == 0) {
     // ======================= TMA producer =======================
-    if (lane == 0) {
+    if (lane == 0 && !p.no_loads) {
       bool ok = true;
       mbar_arrive_expect_tx(BAR_RFULL, C::R_BYTES);
       for (int pn = 0; pn < C::PANELS_D; ++pn)
@@ -310,7 +315,7 @@ __global__ void __launch_bounds__(256, 1)
       auto load_panel = [&](const CUtensorMap* m, int x, int y, int hh) -> bool {
         const int st = cnt % NST;
         const uint32_t ph = (cnt / NST) & 1u;
-        if (!mbar_wait(BAR_EMPTY(st), ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_RING_EMPTY)) return false;
+        if (!mbar_wait(BAR_EMPTY(st), ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_RING_EMPTY, p.wait_limit)) return false;
         mbar_arrive_expect_tx(BAR_FULL(st), C::STAGE_BYTES);
         tma_load_4d(smem_u32(sRing + st * C::STAGE_BYTES), m, BAR_FULL(st), x, y, hh, b);
         ++cnt;
@@ -341,14 +346,14 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp == 1) {
     // ======================= MMA issuer =======================
     if (lane == 0) {
-      bool ok = mbar_wait(BAR_RFULL, 0, abort_flag, p.status, ST_TIMEOUT_RESIDENT);
+      bool ok = mbar_wait(BAR_RFULL, 0, abort_flag, p.status, ST_TIMEOUT_RESIDENT, p.wait_limit);
       tc_fence_after();
       const uint32_t aR1 = smem_u32(sR1), aR2 = smem_u32(sR2), aRing = smem_u32(sRing), aP = smem_u32(sP);
       uint32_t cnt = 0;
       auto scores_from = [&](uint32_t aR, uint32_t d_tmem) -> bool {
         for (int pn = 0; pn < C::PANELS_D; ++pn) {
           const int st = cnt % NST;
-          if (!mbar_wait(BAR_FULL(st), (cnt / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL))
+          if (!mbar_wait(BAR_FULL(st), (cnt / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL, p.wait_limit))
             return false;
           tc_fence_after();
 #pragma unroll
@@ -373,10 +378,10 @@ __global__ void __launch_bounds__(256, 1)
       };
       auto issue_acc = [&](int i) -> bool {
         const int sb = i % NS;
-        if (!mbar_wait(BAR_PREADY(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY)) return false;
+        if (!mbar_wait(BAR_PREADY(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY, p.wait_limit)) return false;
         for (int j = 0; j < C::PANELS_Y; ++j) {
           const int st = (cnt + j) % NST;
-          if (!mbar_wait(BAR_FULL(st), ((cnt + j) / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL))
+          if (!mbar_wait(BAR_FULL(st), ((cnt + j) / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL, p.wait_limit))
             return false;
         }
         tc_fence_after();
@@ -463,7 +468,7 @@ __global__ void __launch_bounds__(256, 1)
 
     for (int i = 0; i < n_items && ok; ++i) {
       const int sb = i % NS;
-      ok = mbar_wait(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
+      ok = mbar_wait(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES, p.wait_limit);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
@@ -527,7 +532,7 @@ __global__ void __launch_bounds__(256, 1)
         }
         l_run = l_run * alpha + sum;
         if (__any_sync(0xffffffffu, rescale)) {
-          ok = mbar_wait(BAR_ACC, (i - 1) & 1u, abort_flag, p.status, ST_TIMEOUT_ACC);
+          ok = mbar_wait(BAR_ACC, (i - 1) & 1u, abort_flag, p.status, ST_TIMEOUT_ACC, p.wait_limit);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
           tc_fence_after();
@@ -626,7 +631,7 @@ __global__ void __launch_bounds__(256, 1)
 
     // ---------------- epilogue ----------------
     if (ok && n_items > 0) {
-      ok = mbar_wait(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
+      ok = mbar_wait(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC, p.wait_limit);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok && n_items > 0) {

@@ -207,7 +207,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
 
   if (warp == 0) {
     // ======================= TMA producer (both CTAs) =======================
-    if (lane == 0) {
+    if (lane == 0 && !p.no_loads) {
       bool ok = true;
       if (leader) mbar_arrive_expect_tx(BAR_RFULL, 2 * C::R_BYTES);
       const uint32_t rfull_l = mapa_shared(BAR_RFULL, 0);
@@ -223,7 +223,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
         st = cnt % NST;
         const uint32_t ph = (cnt / NST) & 1u;
         const long long t0 = tick();
-        const bool got = mbar_wait_cluster(BAR_EMPTY(st), ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_RING_EMPTY);
+        const bool got = mbar_wait_cluster(BAR_EMPTY(st), ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_RING_EMPTY, p.wait_limit);
         tock(WC_PRODUCER_EMPTY, t0);
         if (!got) return false;
         if (leader) mbar_arrive_expect_tx(BAR_FULL(st), 2 * C::STAGE_BYTES);
@@ -285,7 +285,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
   } else if (warp == 1) {
     // ======================= MMA issuer (leader CTA only) =======================
     if (leader && lane == 0) {
-      bool ok = mbar_wait_cluster(BAR_RFULL, 0, abort_flag, p.status, ST_TIMEOUT_RESIDENT);
+      bool ok = mbar_wait_cluster(BAR_RFULL, 0, abort_flag, p.status, ST_TIMEOUT_RESIDENT, p.wait_limit);
       tc_fence_after();
       const uint32_t aR1 = smem_u32(sR1), aR2 = smem_u32(sR2), aRing = smem_u32(sRing), aP = smem_u32(sP);
       uint32_t cnt = 0;
@@ -302,7 +302,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
         for (int s = 0; s < C::C_STAGES; ++s) {
           const int st = cnt % NST;
           const long long t0 = tick();
-          const bool got = mbar_wait_cluster(BAR_FULL(st), (cnt / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL);
+          const bool got = mbar_wait_cluster(BAR_FULL(st), (cnt / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL, p.wait_limit);
           tock(WC_MMA_FULL_SCORES, t0);
           if (!got) return false;
           tc_fence_after();
@@ -334,7 +334,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
       auto issue_acc = [&](int i) -> bool {
         const int sb = i % NS;
         long long t0 = tick();
-        if (!mbar_wait_cluster(BAR_PREADY(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY))
+        if (!mbar_wait_cluster(BAR_PREADY(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY, p.wait_limit))
           return false;
         tock(WC_MMA_PREADY, t0);
         // Accumulate operand stages (both panels of one instruction g and
@@ -348,7 +348,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
           for (int hh = 0; hh < C::YH; ++hh) {
             const uint32_t c2 = cnt + g * C::YH + hh;
             t0 = tick();
-            if (!mbar_wait_cluster(BAR_FULL(c2 % NST), (c2 / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL))
+            if (!mbar_wait_cluster(BAR_FULL(c2 % NST), (c2 / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL, p.wait_limit))
               return false;
             tock(WC_MMA_FULL_Y, t0);
             tc_fence_after();
@@ -382,7 +382,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
         for (int i = 0; i < n_items && ok; ++i) {
           if (i + 1 < n_items) {
             const long long t0 = tick();
-            ok = mbar_wait_cluster(BAR_SFREE(0), i & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY);
+            ok = mbar_wait_cluster(BAR_SFREE(0), i & 1u, abort_flag, p.status, ST_TIMEOUT_PREADY, p.wait_limit);
             tock(WC_MMA_PREADY, t0);
             if (ok) {
               tc_fence_after();
@@ -480,7 +480,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
         const int cb = item_col0(i) + half * (BN / 2);
         const long long t_w = tick();
         if (ok) {
-          ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
+          ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES, p.wait_limit);
           ok = __all_sync(0xffffffffu, ok);
         }
         tock(WC_ROW_SFULL, t_w);
@@ -565,7 +565,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
         if (__any_sync(0xffffffffu, rescale)) {
           // O's rows are rescaled in place once the previous item's P V
           // MMAs have landed (this thread's quadrant, all ACC_COLS columns).
-          ok = mbar_wait_cluster(BAR_ACC, (i - 1) & 1u, abort_flag, p.status, ST_TIMEOUT_ACC);
+          ok = mbar_wait_cluster(BAR_ACC, (i - 1) & 1u, abort_flag, p.status, ST_TIMEOUT_ACC, p.wait_limit);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) continue;
           tc_fence_after();
@@ -601,7 +601,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
 #pragma unroll
       for (int pt = 0; pt < 2 * RW; ++pt) l_tot += xl[pt * M + row];
       if (ok && n_items > 0) {
-        ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
+        ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC, p.wait_limit);
         ok = __all_sync(0xffffffffu, ok);
       }
       if (ok && n_items > 0) {
@@ -683,7 +683,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
         // dQ / dK: wait for S only; dP is waited for after P is computed.
         if (ok) {
           ok = mbar_wait_cluster(C::HAS_DP ? BAR_SREADY(sb) : BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status,
-                                 ST_TIMEOUT_SCORES);
+                                 ST_TIMEOUT_SCORES, p.wait_limit);
           ok = __all_sync(0xffffffffu, ok);
         }
         tock(WC_ROW_SFULL, t_w);
@@ -731,7 +731,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
           // item: wait for its accumulate MMAs (with EARLY_S, S-ready no longer
           // implies them) and for its TMA store to have read it.
           if (C::EARLY_S && i > 0 && ok) {
-            ok = mbar_wait_cluster(BAR_ACC, (i - 1) & 1u, abort_flag, p.status, ST_TIMEOUT_ACC);
+            ok = mbar_wait_cluster(BAR_ACC, (i - 1) & 1u, abort_flag, p.status, ST_TIMEOUT_ACC, p.wait_limit);
             ok = __all_sync(0xffffffffu, ok);
           }
           if (tid0) bulk_wait_read0();
@@ -745,7 +745,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
           if (tid0 && ok) store_block(sb, ws_blk0 + i);
         }
         if (C::HAS_DP && ok) {
-          ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES);
+          ok = mbar_wait_cluster(BAR_SFULL(sb), (i / NS) & 1u, abort_flag, p.status, ST_TIMEOUT_SCORES, p.wait_limit);
           ok = __all_sync(0xffffffffu, ok);
           if (ok) tc_fence_after();
         }
@@ -797,7 +797,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
       // ---------------- epilogue ----------------
       const long long t_epi = tick();
       if (ok && n_items > 0) {
-        ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC);
+        ok = mbar_wait_cluster(BAR_FINAL, 0, abort_flag, p.status, ST_TIMEOUT_ACC, p.wait_limit);
         ok = __all_sync(0xffffffffu, ok);
       }
       if (ok && n_items > 0) {

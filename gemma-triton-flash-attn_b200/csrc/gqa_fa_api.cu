@@ -124,6 +124,10 @@ int bind_device(cudaStream_t stream) {
 
 // Diagnostics buffer (WC_NUM counters) set by gqafa_set_wait_counters; null = off.
 std::atomic<unsigned long long*> g_prof_buffer{nullptr};
+// Test knobs set by gqafa_set_test_waits: the launches' wait bound and the
+// switch that keeps the TMA producers idle.
+std::atomic<long long> g_wait_limit{WAIT_LIMIT_CYCLES};
+std::atomic<int> g_no_loads{0};
 
 int* status_ptr() {
   static std::mutex mu;
@@ -248,6 +252,8 @@ KParams base_params(const Problem& pr) {
   p.scale_log2 = pr.scale * 1.4426950408889634f;
   p.row_begin = pr.row_begin;
   p.row_end = pr.row_end;
+  p.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
+  p.no_loads = g_no_loads.load(std::memory_order_relaxed);
   return p;
 }
 
@@ -718,6 +724,12 @@ extern "C" int gqafa_supported(int head_dim, int dtype) {
 
 extern "C" int gqafa_set_wait_counters(void* device_counters) {
   g_prof_buffer.store(static_cast<unsigned long long*>(device_counters));
+  return GQAFA_OK;
+}
+
+extern "C" int gqafa_set_test_waits(long long wait_limit_cycles, int skip_loads) {
+  g_wait_limit.store(wait_limit_cycles > 0 ? wait_limit_cycles : WAIT_LIMIT_CYCLES);
+  g_no_loads.store(skip_loads ? 1 : 0);
   return GQAFA_OK;
 }
 

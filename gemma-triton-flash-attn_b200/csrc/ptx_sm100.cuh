@@ -2,10 +2,11 @@
 // mbarriers, TMA tiled loads, tcgen05 (TMEM alloc / MMA / commit / ld / st) and
 // the UMMA shared-memory and instruction descriptors.
 //
-// Every wait on an mbarrier is bounded: after WAIT_LIMIT_CYCLES the waiter
-// records an error code in the kernel's status word, raises the CTA-wide abort
-// flag and returns false, so a broken pipeline ends the kernel instead of
-// hanging the GPU.
+// Every wait on an mbarrier is bounded: after `limit` clock cycles (the
+// launch's KParams::wait_limit, WAIT_LIMIT_CYCLES unless a test shortened it)
+// the waiter records an error code in the kernel's status word, raises the
+// CTA-wide abort flag and returns false, so a broken pipeline ends the kernel
+// instead of hanging the GPU.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -61,13 +62,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity. Returns false on timeout
 // or when another role of the CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int code) {
+                                          int* status, int code, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       atomicCAS(status, 0, code);
       return false;
@@ -254,13 +255,13 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 }
 // Bounded wait with cluster-scope acquire (the phase may be completed by the peer CTA).
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                                  int* status, int code) {
+                                                  int* status, int code, long long limit) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       atomicCAS(status, 0, code);
       return false;

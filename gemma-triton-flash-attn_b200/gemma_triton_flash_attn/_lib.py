@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "gqafa_device_status",
     "gqafa_version",
     "gqafa_set_wait_counters",
+    "gqafa_set_test_waits",
 )
 
 _lock = threading.Lock()
@@ -99,6 +100,8 @@ def load():
         lib.gqafa_device_status.restype = _I
         lib.gqafa_set_wait_counters.argtypes = [_P]
         lib.gqafa_set_wait_counters.restype = _I
+        lib.gqafa_set_test_waits.argtypes = [ctypes.c_longlong, _I]
+        lib.gqafa_set_test_waits.restype = _I
         lib.gqafa_version.argtypes = []
         lib.gqafa_version.restype = ctypes.c_char_p
         _lib = lib

@@ -179,6 +179,16 @@ GQAFA_API int gqafa_device_status(int device, int reset);
  * warps' elementwise work, [6] epilogue, [7] CTA lifetime, [8] CTA count. */
 GQAFA_API int gqafa_set_wait_counters(void* device_counters);
 
+/* Test knob (no counterpart in the reference, whose Triton kernels have no
+ * bounded waits): every mbarrier wait of later launches gives up after
+ * `wait_limit_cycles` clock cycles (<= 0 restores the default of 2e9, about
+ * one second), and with `skip_loads` != 0 the kernels' TMA producers issue
+ * nothing, so every wait runs into that bound. A timed-out launch records a
+ * non-zero code in the status word (gqafa_device_status), frees its tensor
+ * memory and returns; its outputs are undefined. Used by the tests of the
+ * timeout path; process-wide, not for production use. */
+GQAFA_API int gqafa_set_test_waits(long long wait_limit_cycles, int skip_loads);
+
 /* Library version string. */
 GQAFA_API const char* gqafa_version(void);
 

@@ -129,8 +129,9 @@ def torch_ref(q, k, v, do, causal, slide, scale=None, chunk=1024, need_grad=True
 
 
 def metrics(x, ref):
-    x = x.detach().float().cpu().reshape(-1).double()
-    r = ref.detach().float().cpu().reshape(-1).double()
+    """(max-abs difference, cosine similarity), in float64 on x's device."""
+    x = x.detach().reshape(-1).double()
+    r = ref.detach().to(x.device).reshape(-1).double()
     max_abs = (x - r).abs().max().item() if x.numel() else 0.0
     denom = (x.norm() * r.norm()).item()
     cos = (x @ r).item() / denom if denom > 0 else 1.0
@@ -165,8 +166,8 @@ def assert_close(name, x, ref, atol=ATOL, cos_min=COS_MIN, emulated=None, magnit
     (e.g. dQ of a one-token sequence); then max-abs <= atol alone applies.
     """
     assert torch.isfinite(x.float()).all(), f"{name}: non-finite values"
-    xf = x.detach().float().cpu()
-    rf = ref.detach().float().cpu()
+    xf = x.detach().float()
+    rf = ref.detach().float().to(xf.device)
     max_abs, cos = metrics(xf, rf)
     negligible = rf.abs().max().item() < 1e-3
     if negligible:
@@ -184,7 +185,7 @@ def assert_close(name, x, ref, atol=ATOL, cos_min=COS_MIN, emulated=None, magnit
             return "B", max_abs, cos
         msgs.append(f"B: excess over storage rounding {excess:.3e}")
         if emulated is not None:
-            ef = emulated.detach().float().cpu()
+            ef = emulated.detach().float().to(xf.device)
             e_abs, e_cos = metrics(xf, ef)
             e_excess = ((xf - ef).abs() - half_ulp(ef, x.dtype)).max().item()
             if e_excess <= atol and e_cos >= cos_min and cos >= cos_min:
@@ -192,7 +193,7 @@ def assert_close(name, x, ref, atol=ATOL, cos_min=COS_MIN, emulated=None, magnit
                 return "C", max_abs, cos
             msgs.append(f"C: vs rounding-emulated fp32 max_abs={e_abs:.3e} excess={e_excess:.3e} cos={e_cos:.6f}")
         if magnitude is not None:
-            mf = magnitude.detach().float().cpu()
+            mf = magnitude.detach().float().to(xf.device)
             bound = atol + half_ulp(rf, x.dtype) + 2 * UNIT_ROUNDOFF[x.dtype] * mf
             worst = ((xf - rf).abs() - bound).max().item()
             if worst <= 0 and cos >= cos_min:

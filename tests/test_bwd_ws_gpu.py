@@ -115,3 +115,70 @@ def test_workspace_limit_splits_over_kv_heads(monkeypatch, D):
     torch.cuda.synchronize()
     for x, y in zip(whole, split):
         assert torch.equal(x, y)
+
+
+def test_workspace_split_b1_uneven_kv_groups(monkeypatch):
+    """B=1 with H_KV=5 (not a power of two): the split over KV heads starts at
+    H_KV // 2 = 2 heads per group, leaving a last group of one; the gradients
+    are bitwise those of the whole-workspace run."""
+    B, Hq, Hkv, N, D = 1, 10, 5, 320, 512
+    q, k, v, do = (t.to(DEV) for t in make_inputs(B, Hq, Hkv, N, D, seed=9))
+    scale = 1 / math.sqrt(D)
+    o, lse = _fwd(q, k, v, True, 0, scale, True)
+    whole = _bwd(q, k, v, o, lse, do, True, 0, scale)
+    size = bwd_workspace_size(B, Hq, Hkv, N, D, True, 0)
+    monkeypatch.setenv("GQAFA_BWD_WORKSPACE_LIMIT", str(2 * (size // Hkv)))  # groups of 2, 2, 1 KV heads
+    split = _bwd(q, k, v, o, lse, do, True, 0, scale)
+    torch.cuda.synchronize()
+    for x, y in zip(whole, split):
+        assert torch.equal(x, y)
+
+
+RECOMPUTE_CASES = [
+    # (B, Hq, Hkv, N, D, causal, window, dtype)
+    (1, 8, 2, 700, 512, True, 0, torch.bfloat16),
+    (2, 4, 4, 257, 512, False, 0, torch.float16),
+    (1, 16, 8, 1500, 256, True, 400, torch.float16),
+    (1, 4, 1, 513, 256, True, 0, torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("case", RECOMPUTE_CASES, ids=lambda c: f"B{c[0]}H{c[1]}x{c[2]}N{c[3]}D{c[4]}w{c[6]}")
+def test_recompute_backward_matches_fp32(case, monkeypatch):
+    """The recomputing backward (gqafa_bwd: dQ + delta, dK, dV kernels), which
+    the memory fallback, the row-range entries and the no-alloc entry run,
+    held directly to the fp32 reference."""
+    B, Hq, Hkv, N, D, causal, window, dt = case
+    q, k, v, do = make_inputs(B, Hq, Hkv, N, D, dt, 0.5, seed=21, device=DEV)
+    scale = 1 / math.sqrt(D)
+    o, lse = _fwd(q, k, v, causal, window, scale, True)
+    monkeypatch.setenv("GQAFA_BWD_WORKSPACE_LIMIT", "0")
+    got = _bwd(q, k, v, o, lse, do, causal, window, scale)
+    torch.cuda.synchronize()
+    ref = torch_ref(q, k, v, do, causal, window, scale)
+    emu = torch_ref(q, k, v, do, causal, window, scale, emulate=True)
+    mag = torch_ref(q, k, v, do, causal, window, scale, magnitudes=True)
+    for i, name in ((2, "dQ"), (3, "dK"), (4, "dV")):
+        assert_close(f"recompute {case} {name}", got[i - 2], ref[i], emulated=emu[i], magnitude=mag[i])
+
+
+def test_noalloc_backward_matches_fp32():
+    """gqafa_bwd_noalloc (delta kept in the library's fixed scratch) held
+    directly to the fp32 reference, not only to gqafa_bwd."""
+    B, Hq, Hkv, N, D, dt = 1, 8, 2, 600, 512, torch.bfloat16
+    q, k, v, do = make_inputs(B, Hq, Hkv, N, D, dt, 0.5, seed=31, device=DEV)
+    scale = 1 / math.sqrt(D)
+    o, lse = _fwd(q, k, v, True, 0, scale, True)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    st = _lib.strides_arg
+    _lib.check(_lib.load().gqafa_bwd_noalloc(
+        q.data_ptr(), st(q.stride()), k.data_ptr(), st(k.stride()), v.data_ptr(), st(v.stride()),
+        o.data_ptr(), st(o.stride()), do.data_ptr(), st(do.stride()), lse.data_ptr(),
+        dq.data_ptr(), st(dq.stride()), dk.data_ptr(), st(dk.stride()), dv.data_ptr(), st(dv.stride()),
+        B, Hq, Hkv, N, D, scale, 1, 0, _lib.GQAFA_DTYPE_BF16, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    ref = torch_ref(q, k, v, do, True, 0, scale)
+    emu = torch_ref(q, k, v, do, True, 0, scale, emulate=True)
+    mag = torch_ref(q, k, v, do, True, 0, scale, magnitudes=True)
+    for i, name, x in ((2, "dQ", dq), (3, "dK", dk), (4, "dV", dv)):
+        assert_close(f"no-alloc {name}", x, ref[i], emulated=emu[i], magnitude=mag[i])
