@@ -45,6 +45,10 @@ enum Role : int { ROLE_FWD = 0, ROLE_DQ = 1, ROLE_DK = 2, ROLE_DV = 3 };
 
 struct KParams {
   int B, Hq, Hkv, N, G;
+  // Key length and the query rows' offset into it: query row r sits at key
+  // position r + qoff (qoff = Nk - N, the last N positions of a KV cache).
+  // The backward runs with Nk == N and qoff == 0.
+  int Nk, qoff;
   int causal, window;  // window > 0 only meaningful with causal (reference semantics)
   float scale, scale_log2;
   int num_row_tiles;  // row tiles in this launch
@@ -161,12 +165,13 @@ struct Cfg {
 };
 
 // The columns a row attends form one interval [lo, hi) of absolute indices:
-// for a query row q, keys max(0, q-W+1) .. min(q, N-1) (causal) or 0 .. N-1;
-// for a key row k, queries k .. min(k+W-1, N-1) (causal) or 0 .. N-1. Masking
-// is then one unsigned compare per element (an element test inside the
-// unrolled loops costs far more).
-__device__ __forceinline__ void attended_interval(bool row_is_query, int row, int N, int causal, int window,
-                                                  int& lo, int& hi) {
+// for a query row q at key position q' = q + qoff, keys max(0, q'-W+1) .. q'
+// (causal) or 0 .. Nk-1; for a key row k (backward, Nk == N), queries
+// k .. min(k+W-1, N-1) (causal) or 0 .. N-1. Masking is then one unsigned
+// compare per element (an element test inside the unrolled loops costs far
+// more).
+__device__ __forceinline__ void attended_interval(bool row_is_query, int row, int N, int Nk, int qoff, int causal,
+                                                  int window, int& lo, int& hi) {
   if (row >= N) {
     lo = 0;
     hi = 0;
@@ -174,10 +179,10 @@ __device__ __forceinline__ void attended_interval(bool row_is_query, int row, in
   }
   if (!causal) {
     lo = 0;
-    hi = N;
+    hi = row_is_query ? Nk : N;
   } else if (row_is_query) {
-    lo = window > 0 ? max(0, row - window + 1) : 0;
-    hi = row + 1;
+    lo = window > 0 ? max(0, row + qoff - window + 1) : 0;
+    hi = row + qoff + 1;
   } else {
     lo = row;
     hi = window > 0 ? min(N, row + window) : N;
@@ -188,6 +193,44 @@ __device__ __forceinline__ void attended_interval(bool row_is_query, int row, in
 // (unsigned)(c - lo_rel) < span.
 __device__ __forceinline__ unsigned span_of(int lo_rel, int hi_rel) {
   return hi_rel > lo_rel ? static_cast<unsigned>(hi_rel - lo_rel) : 0u;
+}
+
+// This lane's part of dot(a, b) over one row of D 16-bit values: 16-byte
+// loads for D >= 256 (8 values per lane per pass), 8-byte loads at D = 128 and
+// 4-byte loads at D = 64, so the warp reads the row in coalesced passes. The
+// caller reduces over the warp.
+template <int D, bool BF16>
+__device__ __forceinline__ float row_dot(const uint16_t* a, const uint16_t* b, int lane) {
+  float acc = 0.f;
+  if constexpr (D >= 256) {
+#pragma unroll
+    for (int it = 0; it < D / 256; ++it) {
+      const uint4 x = *reinterpret_cast<const uint4*>(a + it * 256 + lane * 8);
+      const uint4 y = *reinterpret_cast<const uint4*>(b + it * 256 + lane * 8);
+      const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, yw[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc += unpack_lo<BF16>(xw[e]) * unpack_lo<BF16>(yw[e]);
+        acc += unpack_hi<BF16>(xw[e]) * unpack_hi<BF16>(yw[e]);
+      }
+    }
+  } else if constexpr (D == 128) {
+    const uint2 x = *reinterpret_cast<const uint2*>(a + lane * 4);
+    const uint2 y = *reinterpret_cast<const uint2*>(b + lane * 4);
+    const uint32_t xw[2] = {x.x, x.y}, yw[2] = {y.x, y.y};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      acc += unpack_lo<BF16>(xw[e]) * unpack_lo<BF16>(yw[e]);
+      acc += unpack_hi<BF16>(xw[e]) * unpack_hi<BF16>(yw[e]);
+    }
+  } else {
+    static_assert(D == 64, "head_dim");
+    const uint32_t xw = *reinterpret_cast<const uint32_t*>(a + lane * 2);
+    const uint32_t yw = *reinterpret_cast<const uint32_t*>(b + lane * 2);
+    acc += unpack_lo<BF16>(xw) * unpack_lo<BF16>(yw);
+    acc += unpack_hi<BF16>(xw) * unpack_hi<BF16>(yw);
+  }
+  return acc;
 }
 
 template <bool BF16>
@@ -252,8 +295,8 @@ __global__ void __launch_bounds__(256, 1)
 
   int jlo, jn, n_items;
   if constexpr (C::ROWS_ARE_Q) {
-    const int kv_hi = p.causal ? min(N, r0 + M) : N;
-    const int kv_lo = swa ? max(0, r0 - p.window + 1) : 0;
+    const int kv_hi = p.causal ? min(p.Nk, r0 + M + p.qoff) : p.Nk;
+    const int kv_lo = swa ? max(0, r0 + p.qoff - p.window + 1) : 0;
     jlo = kv_lo / BN;
     jn = (kv_hi + BN - 1) / BN - jlo;
     n_items = jn;
@@ -439,19 +482,7 @@ __global__ void __launch_bounds__(256, 1)
       for (int r = q4; r < M; r += 4) {
         const int q = r0 + r;
         float acc = 0.f;
-        if (q < N) {
-#pragma unroll
-          for (int it = 0; it < C::D / 256; ++it) {
-            const uint4 a = *reinterpret_cast<const uint4*>(Og + q * p.o_sn + it * 256 + lane * 8);
-            const uint4 c = *reinterpret_cast<const uint4*>(dOg + q * p.do_sn + it * 256 + lane * 8);
-            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              acc += unpack_lo<C::BF16>(aw[e]) * unpack_lo<C::BF16>(cw[e]);
-              acc += unpack_hi<C::BF16>(aw[e]) * unpack_hi<C::BF16>(cw[e]);
-            }
-          }
-        }
+        if (q < N) acc = row_dot<C::D, C::BF16>(Og + q * p.o_sn, dOg + q * p.do_sn, lane);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         if (lane == 0) {
@@ -477,14 +508,14 @@ __global__ void __launch_bounds__(256, 1)
       const uint32_t dp_col = C::S_COL0 + (NS + sb) * BN;
       bool need_mask;
       if constexpr (C::ROWS_ARE_Q) {
-        need_mask = (c0 + BN > N) || (p.causal && c0 + BN - 1 > r0) ||
-                    (swa && r0 + M - 1 - c0 >= p.window);
+        need_mask = (c0 + BN > p.Nk) || (p.causal && c0 + BN - 1 > r0 + p.qoff) ||
+                    (swa && r0 + p.qoff + M - 1 - c0 >= p.window);
       } else {
         need_mask = (c0 + BN > N) || (p.causal && r0 + M - 1 > c0) ||
                     (swa && c0 + BN - 1 - r0 >= p.window);
       }
       int lo_abs, hi_abs;
-      attended_interval(C::ROWS_ARE_Q, r0 + srow, N, p.causal, p.window, lo_abs, hi_abs);
+      attended_interval(C::ROWS_ARE_Q, r0 + srow, N, p.Nk, p.qoff, p.causal, p.window, lo_abs, hi_abs);
       const int lo_rel = lo_abs - c0;
       const unsigned span = span_of(lo_rel, hi_abs - c0);
       auto valid = [&](int c) { return static_cast<unsigned>(c - lo_rel) < span; };

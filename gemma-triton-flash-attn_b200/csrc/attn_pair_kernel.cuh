@@ -154,8 +154,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
 
   int jlo, jn, n_items;
   if constexpr (C::ROWS_ARE_Q) {
-    const int kv_hi = p.causal ? min(N, pr0 + MP) : N;
-    const int kv_lo = swa ? max(0, pr0 - p.window + 1) : 0;
+    const int kv_hi = p.causal ? min(p.Nk, pr0 + MP + p.qoff) : p.Nk;
+    const int kv_lo = swa ? max(0, pr0 + p.qoff - p.window + 1) : 0;
     jlo = kv_lo / BN;
     jn = (kv_hi + BN - 1) / BN - jlo;
     n_items = jn;
@@ -431,19 +431,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
       for (int r = rwi; r < M; r += 4 * RW) {
         const int q = r0 + r;
         float acc = 0.f;
-        if (q < N) {
-#pragma unroll
-          for (int it = 0; it < C::D / 256; ++it) {
-            const uint4 a = *reinterpret_cast<const uint4*>(Og + q * p.o_sn + it * 256 + lane * 8);
-            const uint4 c = *reinterpret_cast<const uint4*>(dOg + q * p.do_sn + it * 256 + lane * 8);
-            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              acc += unpack_lo<C::BF16>(aw[e]) * unpack_lo<C::BF16>(cw[e]);
-              acc += unpack_hi<C::BF16>(aw[e]) * unpack_hi<C::BF16>(cw[e]);
-            }
-          }
-        }
+        if (q < N) acc = row_dot<C::D, C::BF16>(Og + q * p.o_sn, dOg + q * p.do_sn, lane);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         if (lane == 0) {
@@ -492,7 +480,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
         // all columns would multiply the code size, and the instruction cache
         // is shared with the MMA-issuing thread.
         int lo_abs, hi_abs;
-        attended_interval(true, r0 + row, N, p.causal, p.window, lo_abs, hi_abs);
+        attended_interval(true, r0 + row, N, p.Nk, p.qoff, p.causal, p.window, lo_abs, hi_abs);
         const int lo_rel = lo_abs - cb;
         const unsigned span = span_of(lo_rel, hi_abs - cb);
         float mx = -INFINITY;
@@ -697,7 +685,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
         if (ok) {
           tc_fence_after();
           int lo_abs, hi_abs;
-          attended_interval(C::ROWS_ARE_Q, r0 + row, N, p.causal, p.window, lo_abs, hi_abs);
+          attended_interval(C::ROWS_ARE_Q, r0 + row, N, p.Nk, p.qoff, p.causal, p.window, lo_abs, hi_abs);
           const int lo_rel = lo_abs - cb;
           const unsigned span = span_of(lo_rel, hi_abs - cb);
 #pragma unroll

@@ -6,6 +6,7 @@
 //                 dQ, dK   M=128 BN=128, single-buffered scores (TMEM: 256+128+128)
 //                 dV       M=128 BN=128, double-buffered scores
 //   head_dim 512  all      CTA pairs (attn_pair_kernel.cuh), 64 rows per CTA, BN=256
+//   head_dim 64, 128       1-CTA kernels, M=128 BN=128, recomputing backward
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -186,6 +187,16 @@ template <bool BF16> using Fwd256 = Cfg<ROLE_FWD, 128, 256, 256, 128, 2, 8, 4, B
 template <bool BF16> using Dq256 = Cfg<ROLE_DQ, 128, 256, 256, 128, 1, 6, 2, BF16>;
 template <bool BF16> using Dk256 = PairCfg<ROLE_DK, 256, 128, 2, 4, BF16>;  // pair: faster than 1-CTA here
 template <bool BF16> using Dv256 = Cfg<ROLE_DV, 128, 256, 256, 128, 2, 8, 4, BF16>;
+// head_dim 64 and 128: the 1-CTA template throughout (the whole accumulator
+// and double-buffered scores fit one SM's TMEM); the backward recomputes.
+template <bool BF16> using Fwd128 = Cfg<ROLE_FWD, 128, 128, 128, 128, 2, 8, 2, BF16>;
+template <bool BF16> using Dq128 = Cfg<ROLE_DQ, 128, 128, 128, 128, 1, 8, 2, BF16>;
+template <bool BF16> using Dk128 = Cfg<ROLE_DK, 128, 128, 128, 128, 1, 8, 2, BF16>;
+template <bool BF16> using Dv128 = Cfg<ROLE_DV, 128, 128, 128, 128, 2, 8, 2, BF16>;
+template <bool BF16> using Fwd64 = Cfg<ROLE_FWD, 128, 64, 64, 128, 2, 8, 1, BF16>;
+template <bool BF16> using Dq64 = Cfg<ROLE_DQ, 128, 64, 64, 128, 1, 8, 1, BF16>;
+template <bool BF16> using Dk64 = Cfg<ROLE_DK, 128, 64, 64, 128, 1, 8, 1, BF16>;
+template <bool BF16> using Dv64 = Cfg<ROLE_DV, 128, 64, 64, 128, 2, 8, 1, BF16>;
 // head_dim 512: CTA pairs, PairCfg<ROLE, D, BN, NS, NSTAGES, BF16>. The forward keeps all 512 O
 // columns in TMEM (256 per CTA), so S is computed once per item. 256-column items make
 // every score MMA an N=256 pair instruction (full tensor rate; N=128 pair MMAs run at 70%), at the
@@ -205,6 +216,7 @@ template <bool BF16> using Dkv256 = DkvCfg<256, 7, BF16>;
 
 struct Problem {
   int B, Hq, Hkv, N, D, causal, window;
+  int Nk;  // key length (== N except for the KV-cache forward)
   int row_begin, row_end;  // rows of the row-tile dimension to compute
   float scale;
   bool bf16;
@@ -217,8 +229,9 @@ int check_problem(int B, int Hq, int Hkv, int N, int D, float scale, int causal,
   if (Hq % Hkv != 0) return fail(GQAFA_ERR_INVALID, "H_Q (%d) must be a multiple of H_KV (%d)", Hq, Hkv);
   if (dtype != GQAFA_DTYPE_FP16 && dtype != GQAFA_DTYPE_BF16)
     return fail(GQAFA_ERR_INVALID, "dtype code %d is not fp16 (0) or bf16 (1)", dtype);
-  if (D != 256 && D != 512)
-    return fail(GQAFA_ERR_UNSUPPORTED, "head_dim %d is not implemented on sm_100a (supported: 256, 512)", D);
+  if (D != 64 && D != 128 && D != 256 && D != 512)
+    return fail(GQAFA_ERR_UNSUPPORTED, "head_dim %d is not implemented on sm_100a (supported: 64, 128, 256, 512)",
+                D);
   if (!(scale > 0.f) || !std::isfinite(scale))
     return fail(GQAFA_ERR_INVALID, "softmax_scale must be positive and finite");
   if (window < 0) return fail(GQAFA_ERR_INVALID, "window must be >= 0");
@@ -228,6 +241,7 @@ int check_problem(int B, int Hq, int Hkv, int N, int D, float scale, int causal,
   pr->N = N;
   pr->D = D;
   pr->causal = causal ? 1 : 0;
+  pr->Nk = N;
   // Reference semantics: the window only applies to causal attention and a
   // window covering the whole sequence is plain causal.
   pr->window = (pr->causal && window > 0 && window < N) ? window : 0;
@@ -245,6 +259,8 @@ KParams base_params(const Problem& pr) {
   p.Hq = pr.Hq;
   p.Hkv = pr.Hkv;
   p.N = pr.N;
+  p.Nk = pr.Nk;
+  p.qoff = pr.Nk - pr.N;
   p.G = pr.Hq / pr.Hkv;
   p.causal = pr.causal;
   p.window = pr.window;
@@ -275,8 +291,8 @@ int fwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
     cbox = CF::C_BOX;
     ybox = CF::Y_BOX;
   }
-  if ((rc = encode_map(&maps[2], k, pr.B, pr.N, pr.D, cbox, BF16))) return rc;
-  if ((rc = encode_map(&maps[4], v, pr.B, pr.N, pr.D, ybox, BF16))) return rc;
+  if ((rc = encode_map(&maps[2], k, pr.B, pr.Nk, pr.D, cbox, BF16))) return rc;
+  if ((rc = encode_map(&maps[4], v, pr.B, pr.Nk, pr.D, ybox, BF16))) return rc;
   maps[1] = maps[0];
   maps[3] = maps[2];
   KParams p = base_params(pr);
@@ -479,23 +495,39 @@ static int set_rows(Problem* pr, int row_begin, int row_end) {
 static int fwd_entry(int row_begin, int row_end, const void* q, const long long* q_strides, const void* k,
                      const long long* k_strides, const void* v, const long long* v_strides, void* o,
                      const long long* o_strides, float* lse, int batch, int heads_q, int heads_kv, int seqlen,
-                     int head_dim, float softmax_scale, int causal, int window, int dtype, void* stream) {
+                     int head_dim, float softmax_scale, int causal, int window, int dtype, void* stream,
+                     int seqlen_k = -1) {
   g_last_error.clear();
   Problem pr{};
   int rc;
   if ((rc = check_problem(batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, window, dtype, &pr)))
     return rc;
+  if (seqlen_k >= 0) {
+    if (seqlen_k <= 0) return fail(GQAFA_ERR_INVALID, "key length must be positive");
+    if (pr.causal && seqlen_k < seqlen)
+      return fail(GQAFA_ERR_INVALID,
+                  "causal attention needs key length >= query length (queries are the last %d of %d positions)",
+                  seqlen, seqlen_k);
+    pr.Nk = seqlen_k;
+    pr.window = (pr.causal && window > 0 && window < seqlen_k) ? window : 0;
+  }
   if (row_end < 0) row_end = seqlen;
   if ((rc = set_rows(&pr, row_begin, row_end))) return rc;
   TensorDesc qd, kd, vd, od;
   if ((rc = check_tensor("q", q, q_strides, batch, heads_q, seqlen, head_dim, &qd))) return rc;
-  if ((rc = check_tensor("k", k, k_strides, batch, heads_kv, seqlen, head_dim, &kd))) return rc;
-  if ((rc = check_tensor("v", v, v_strides, batch, heads_kv, seqlen, head_dim, &vd))) return rc;
+  if ((rc = check_tensor("k", k, k_strides, batch, heads_kv, pr.Nk, head_dim, &kd))) return rc;
+  if ((rc = check_tensor("v", v, v_strides, batch, heads_kv, pr.Nk, head_dim, &vd))) return rc;
   if ((rc = check_tensor("o", o, o_strides, batch, heads_q, seqlen, head_dim, &od))) return rc;
   if (lse != nullptr && reinterpret_cast<uintptr_t>(lse) % 4 != 0)
     return fail(GQAFA_ERR_INVALID, "lse must be 4-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = bind_device(st))) return rc;
+  if (pr.D == 64)
+    return pr.bf16 ? fwd_impl<true, Fwd64<true>>(pr, qd, kd, vd, o, od, lse, st)
+                   : fwd_impl<false, Fwd64<false>>(pr, qd, kd, vd, o, od, lse, st);
+  if (pr.D == 128)
+    return pr.bf16 ? fwd_impl<true, Fwd128<true>>(pr, qd, kd, vd, o, od, lse, st)
+                   : fwd_impl<false, Fwd128<false>>(pr, qd, kd, vd, o, od, lse, st);
   if (pr.D == 256)
     return pr.bf16 ? fwd_impl<true, Fwd256<true>>(pr, qd, kd, vd, o, od, lse, st)
                    : fwd_impl<false, Fwd256<false>>(pr, qd, kd, vd, o, od, lse, st);
@@ -509,6 +541,14 @@ extern "C" int gqafa_fwd(const void* q, const long long* q_strides, const void* 
                          float softmax_scale, int causal, int window, int dtype, void* stream) {
   return fwd_entry(0, -1, q, q_strides, k, k_strides, v, v_strides, o, o_strides, lse, batch, heads_q, heads_kv,
                    seqlen, head_dim, softmax_scale, causal, window, dtype, stream);
+}
+
+extern "C" int gqafa_fwd_kv(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+                            const void* v, const long long* v_strides, void* o, const long long* o_strides,
+                            float* lse, int batch, int heads_q, int heads_kv, int seqlen_q, int seqlen_k,
+                            int head_dim, float softmax_scale, int causal, int window, int dtype, void* stream) {
+  return fwd_entry(0, -1, q, q_strides, k, k_strides, v, v_strides, o, o_strides, lse, batch, heads_q, heads_kv,
+                   seqlen_q, head_dim, softmax_scale, causal, window, dtype, stream, seqlen_k);
 }
 
 extern "C" int gqafa_fwd_rows(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
@@ -547,6 +587,17 @@ static int bwd_entry(int stages, int row_begin, int row_end, const void* q, cons
   if (lse == nullptr || delta == nullptr) return fail(GQAFA_ERR_INVALID, "lse and delta must be non-null");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = bind_device(st))) return rc;
+  if (pr.D == 64)
+    return pr.bf16 ? bwd_impl<true, Dq64<true>, Dk64<true>, Dv64<true>>(pr, qd, kd, vd, od, dod, lse, dq, dqd, dk,
+                                                                        dkd, dv, dvd, delta, st, stages)
+                   : bwd_impl<false, Dq64<false>, Dk64<false>, Dv64<false>>(pr, qd, kd, vd, od, dod, lse, dq, dqd,
+                                                                           dk, dkd, dv, dvd, delta, st, stages);
+  if (pr.D == 128)
+    return pr.bf16 ? bwd_impl<true, Dq128<true>, Dk128<true>, Dv128<true>>(pr, qd, kd, vd, od, dod, lse, dq, dqd,
+                                                                           dk, dkd, dv, dvd, delta, st, stages)
+                   : bwd_impl<false, Dq128<false>, Dk128<false>, Dv128<false>>(pr, qd, kd, vd, od, dod, lse, dq,
+                                                                              dqd, dk, dkd, dv, dvd, delta, st,
+                                                                              stages);
   if (pr.D == 256)
     return pr.bf16 ? bwd_impl<true, Dq256<true>, Dk256<true>, Dv256<true>>(pr, qd, kd, vd, od, dod, lse, dq, dqd,
                                                                             dk, dkd, dv, dvd, delta, st, stages)
@@ -719,7 +770,8 @@ extern "C" int gqafa_bwd_noalloc(const void* q, const long long* q_strides, cons
 }
 
 extern "C" int gqafa_supported(int head_dim, int dtype) {
-  return (head_dim == 256 || head_dim == 512) && (dtype == GQAFA_DTYPE_FP16 || dtype == GQAFA_DTYPE_BF16);
+  return (head_dim == 64 || head_dim == 128 || head_dim == 256 || head_dim == 512) &&
+         (dtype == GQAFA_DTYPE_FP16 || dtype == GQAFA_DTYPE_BF16);
 }
 
 extern "C" int gqafa_set_wait_counters(void* device_counters) {

@@ -25,6 +25,7 @@ GQAFA_ERR_CUDA = 3
 # Every symbol include/gqa_fa_b200.h declares.
 EXPORTED_SYMBOLS = (
     "gqafa_fwd",
+    "gqafa_fwd_kv",
     "gqafa_bwd",
     "gqafa_bwd_stage",
     "gqafa_bwd_noalloc",
@@ -69,6 +70,8 @@ def load():
         lib = ctypes.CDLL(LIB_PATH)
         lib.gqafa_fwd.argtypes = [_P, _S, _P, _S, _P, _S, _P, _S, _P, _I, _I, _I, _I, _I, _F, _I, _I, _I, _P]
         lib.gqafa_fwd.restype = _I
+        lib.gqafa_fwd_kv.argtypes = [_P, _S, _P, _S, _P, _S, _P, _S, _P, _I, _I, _I, _I, _I, _I, _F, _I, _I, _I, _P]
+        lib.gqafa_fwd_kv.restype = _I
         lib.gqafa_bwd.argtypes = (
             [_P, _S, _P, _S, _P, _S, _P, _S, _P, _S, _P, _P, _S, _P, _S, _P, _S, _P]
             + [_I, _I, _I, _I, _I, _F, _I, _I, _I, _P]

@@ -106,7 +106,10 @@ def _abi_ready(t: torch.Tensor) -> torch.Tensor:
     return t if ok else t.contiguous()
 
 
-def _check_inputs(q, k, v):
+def _check_inputs(q, k, v, kv_cache=False, causal=False):
+    """Validate q, k, v. kv_cache=True accepts a key length different from the
+    query length (forward only): with causal attention the queries are the
+    last positions of the keys, so the key length must not be shorter."""
     for name, t in (("q", q), ("k", k), ("v", v)):
         if not isinstance(t, torch.Tensor):
             raise TypeError(f"{name} must be a torch.Tensor")
@@ -128,10 +131,13 @@ def _check_inputs(q, k, v):
         raise ValueError(f"k and v shapes differ: {tuple(k.shape)} vs {tuple(v.shape)}")
     if k.shape[0] != b or k.shape[3] != d:
         raise ValueError(f"k/v shape {tuple(k.shape)} incompatible with q {tuple(q.shape)}")
-    if k.shape[2] != n:
+    if k.shape[2] != n and not kv_cache:
         raise ValueError(
-            f"key length {k.shape[2]} != query length {n}: only self-attention is supported"
+            f"key length {k.shape[2]} != query length {n}: only self-attention is supported here "
+            "(attention_flash_gqa takes a longer KV cache)"
         )
+    if kv_cache and causal and k.shape[2] < n:
+        raise ValueError(f"causal attention needs key length {k.shape[2]} >= query length {n}")
     h_kv = k.shape[1]
     if h_q % h_kv != 0:
         raise ValueError(f"H_Q ({h_q}) must be a multiple of H_KV ({h_kv})")
@@ -172,10 +178,11 @@ class _DeviceScope:
 
 def _fwd(q, k, v, causal, window, scale, want_lse, rows=None, out=None):
     """Forward launch. `rows` = (begin, end) computes only those query rows,
-    into the preallocated `out` = (o, lse) (sequence-split multi-GPU path)."""
+    into the preallocated `out` = (o, lse) (sequence-split multi-GPU path).
+    A key length different from the query length runs gqafa_fwd_kv."""
     lib = _lib.load()
     b, h_q, n, d = q.shape
-    h_kv = k.shape[1]
+    h_kv, nk = k.shape[1], k.shape[2]
     q, k, v = _abi_ready(q), _abi_ready(k), _abi_ready(v)
     if out is None:
         o = torch.empty_like(q)  # keeps q's layout (e.g. HF's (B, N, H, D) storage)
@@ -183,7 +190,14 @@ def _fwd(q, k, v, causal, window, scale, want_lse, rows=None, out=None):
         lse = torch.empty((b, h_q, n), dtype=torch.float32, device=q.device) if want_lse else None
     else:
         o, lse = out
-    fn = lib.gqafa_fwd if rows is None else (lambda *a: lib.gqafa_fwd_rows(*a, int(rows[0]), int(rows[1])))
+    if nk != n:
+        if rows is not None:
+            raise ValueError("row ranges need key length == query length")
+        fn = lambda *a: lib.gqafa_fwd_kv(*a[:13], nk, *a[13:])  # noqa: E731
+    elif rows is None:
+        fn = lib.gqafa_fwd
+    else:
+        fn = lambda *a: lib.gqafa_fwd_rows(*a, int(rows[0]), int(rows[1]))  # noqa: E731
     with _DeviceScope(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
         rc = fn(
@@ -350,10 +364,16 @@ def attention_flash_gqa(q, k, v, causal=False, slide_size=0,
                         BLOCK_D=None, num_warps=None, num_stages=None):
     """Inference forward (no LSE, no autograd). Tile arguments are ignored.
 
-    q: (B, H_Q, N, D); k, v: (B, H_KV, N, D). Returns O shaped and typed like q.
+    q: (B, H_Q, N, D); k, v: (B, H_KV, N_k, D). Returns O shaped and typed like q.
+
+    N_k may differ from N (a KV cache, e.g. decoding): with ``causal`` the
+    queries are the last N of the N_k positions (N_k >= N), and a sliding
+    window counts back from each query's position; without ``causal`` every
+    query sees all N_k keys. (The reference reads keys up to N only,
+    attention.py:552-553.)
     """
-    _check_inputs(q, k, v)
-    window = _normalize_window(causal, slide_size, q.shape[2])
+    _check_inputs(q, k, v, kv_cache=True, causal=causal)
+    window = _normalize_window(causal, slide_size, k.shape[2])
     o, _ = _fwd(q, k, v, causal, window, 1.0 / math.sqrt(q.shape[3]), want_lse=False)
     return o
 
@@ -395,9 +415,10 @@ def flash_attn_gqa_forward_with_lse(q, k, v, causal=False, slide_size=0, softmax
     """Forward returning (O, LSE); LSE is fp32 (B, H_Q, N), natural log, scaled.
 
     Not in the reference's public API; used by tests and the multi-GPU path.
+    Accepts a KV cache longer than the queries as attention_flash_gqa does.
     """
-    _check_inputs(q, k, v)
-    window = _normalize_window(causal, slide_size, q.shape[2])
+    _check_inputs(q, k, v, kv_cache=True, causal=causal)
+    window = _normalize_window(causal, slide_size, k.shape[2])
     scale = (1.0 / math.sqrt(q.shape[3])) if softmax_scale is None else float(softmax_scale)
     return _fwd(q, k, v, causal, window, scale, want_lse=True)
 

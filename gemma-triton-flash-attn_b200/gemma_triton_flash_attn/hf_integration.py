@@ -12,7 +12,13 @@ from __future__ import annotations
 
 import torch
 
-from .attention import FlashAttnGQAFunction
+from .attention import FlashAttnGQAFunction, _check_inputs, _fwd, _normalize_window
+
+
+def _kv_cache_forward(q, k, v, causal, slide, scale):
+    _check_inputs(q, k, v, kv_cache=True, causal=causal)
+    o, _ = _fwd(q, k, v, causal, _normalize_window(causal, slide, k.shape[2]), scale, want_lse=False)
+    return o
 
 __all__ = [
     "triton_gqa_attention",
@@ -55,7 +61,15 @@ def triton_gqa_attention(
     scale = scaling if scaling is not None else module.head_dim ** -0.5
     slide = int(sliding_window) if sliding_window else 0
     is_causal = getattr(module, "is_causal", True)
-    out = FlashAttnGQAFunction.apply(query, key, value, is_causal, slide, float(scale))
+    if key.shape[2] != query.shape[2]:
+        # generation with a KV cache: the queries are the last positions of the
+        # cache; forward only (the reference reads the wrong key range here,
+        # attention.py:552-553)
+        if torch.is_grad_enabled() and (query.requires_grad or key.requires_grad or value.requires_grad):
+            raise NotImplementedError("triton_gqa_attention: no backward with a KV cache longer than the queries")
+        out = _kv_cache_forward(query, key, value, is_causal, slide, float(scale))
+    else:
+        out = FlashAttnGQAFunction.apply(query, key, value, is_causal, slide, float(scale))
     out = out.transpose(1, 2).contiguous()
     return out, None
 

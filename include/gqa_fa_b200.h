@@ -20,6 +20,8 @@
  *     be 1, the others multiples of 8 elements (16 bytes), pointers 16-byte
  *     aligned. Transposed views such as HF's [B, N, H, D] storage are accepted
  *     without a copy.
+ *   - head_dim is 64, 128, 256 or 512 (the reference accepts powers of two up to
+ *     512, docs/api.md:63); other values return GQAFA_ERR_UNSUPPORTED.
  *   - causal != 0 applies k <= q. window > 0 additionally applies q - k < window,
  *     and only when causal != 0 (attention.py:289-293, 347-356). window >= N is
  *     treated as full causal (attention.py:1442-1443).
@@ -62,6 +64,21 @@ GQAFA_API int gqafa_fwd(const void* q, const long long* q_strides, const void* k
               const void* v, const long long* v_strides, void* o, const long long* o_strides, float* lse,
               int batch, int heads_q, int heads_kv, int seqlen, int head_dim, float softmax_scale,
               int causal, int window, int dtype, void* stream);
+
+/* Forward with a key length different from the query length (a KV cache:
+ * decode or chunked prefill). q and o are [B, H_Q, seqlen_q, D], k and v
+ * [B, H_KV, seqlen_k, D], lse (may be NULL) [B, H_Q, seqlen_q]. With causal
+ * != 0 the queries are the last seqlen_q of the seqlen_k positions (query row
+ * r sits at key position r + seqlen_k - seqlen_q, so seqlen_k >= seqlen_q is
+ * required) and a window counts back from that position; without causal every
+ * query sees all seqlen_k keys. Replaces the same forward launch as gqafa_fwd
+ * (flash_attn/attention.py:583-603): the reference takes the key length from q
+ * (attention.py:552-553) and so reads the wrong range of a longer cache; this
+ * entry takes both lengths. There is no backward for seqlen_k != seqlen_q. */
+GQAFA_API int gqafa_fwd_kv(const void* q, const long long* q_strides, const void* k, const long long* k_strides,
+              const void* v, const long long* v_strides, void* o, const long long* o_strides, float* lse,
+              int batch, int heads_q, int heads_kv, int seqlen_q, int seqlen_k, int head_dim,
+              float softmax_scale, int causal, int window, int dtype, void* stream);
 
 /* Backward. Reads q, k, v, o, dout and lse; writes dq, dk, dv and delta. */
 GQAFA_API int gqafa_bwd(const void* q, const long long* q_strides, const void* k, const long long* k_strides,

@@ -38,7 +38,8 @@ def test_library_is_in_tree_and_built_for_sm100a():
 def test_supported_and_version():
     lib = _lib.load()
     assert lib.gqafa_supported(512, 1) == 1 and lib.gqafa_supported(256, 0) == 1
-    assert lib.gqafa_supported(128, 1) == 0 and lib.gqafa_supported(512, 7) == 0
+    assert lib.gqafa_supported(128, 1) == 1 and lib.gqafa_supported(64, 0) == 1
+    assert lib.gqafa_supported(96, 1) == 0 and lib.gqafa_supported(32, 1) == 0 and lib.gqafa_supported(512, 7) == 0
     assert "sm_100a" in _lib.version()
 
 
@@ -58,7 +59,7 @@ def _fwd(**over):
 
 @pytest.mark.parametrize("over,code,msg", [
     (dict(Hq=30), _lib.GQAFA_ERR_INVALID, "multiple of H_KV"),
-    (dict(D=128), _lib.GQAFA_ERR_UNSUPPORTED, "head_dim 128"),
+    (dict(D=96), _lib.GQAFA_ERR_UNSUPPORTED, "head_dim 96"),
     (dict(dtype=3), _lib.GQAFA_ERR_INVALID, "dtype"),
     (dict(N=0), _lib.GQAFA_ERR_INVALID, "positive"),
     (dict(scale=0.0), _lib.GQAFA_ERR_INVALID, "softmax_scale"),
@@ -75,7 +76,7 @@ def test_fwd_validation(over, code, msg):
 
 
 def test_check_maps_codes_to_python_exceptions():
-    assert _fwd(D=128) == _lib.GQAFA_ERR_UNSUPPORTED
+    assert _fwd(D=96) == _lib.GQAFA_ERR_UNSUPPORTED
     with pytest.raises(NotImplementedError):
         _lib.check(_lib.GQAFA_ERR_UNSUPPORTED)
     assert _fwd(Hq=30) == _lib.GQAFA_ERR_INVALID
@@ -112,5 +113,6 @@ def test_bwd_workspace_size(n, causal, window):
     want = 2 * 2 * 8 * _blocks_per_head(n, causal, w) * 128 * 256 * 2
     assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 512, int(causal), window) == want
     assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 256, int(causal), window) == want
-    assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 128, int(causal), window) == -1
+    assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 128, int(causal), window) == 0  # recomputing backward
+    assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 96, int(causal), window) == -1
     assert lib.gqafa_bwd_workspace_size(2, 8, 3, n, 512, int(causal), window) == -1

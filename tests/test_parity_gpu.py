@@ -55,7 +55,8 @@ def ref_set(q, k, v, do, causal, slide, scale=None):
 
 
 # ----------------------------------------------------------------- golden
-KERNEL_GOLDEN = [p for p in golden_cases() if "kernel_" in p]
+# every fixture whose head_dim the kernels implement (64, 128, 256, 512)
+KERNEL_GOLDEN = [p for p in golden_cases() if int(np.load(p)["meta"][4]) in (64, 128, 256, 512)]
 
 
 @pytest.mark.parametrize("path", KERNEL_GOLDEN, ids=lambda p: p.split("/")[-1][:-4])
@@ -183,7 +184,7 @@ def test_validation_errors_on_gpu():
     with pytest.raises(ValueError, match="multiple of H_KV"):
         gfa.flash_attn_gqa_train(q[:, :3], k, v)
     with pytest.raises(NotImplementedError):
-        gfa.flash_attn_gqa_train(q[..., :128].contiguous(), k[..., :128].contiguous(), v[..., :128].contiguous())
+        gfa.flash_attn_gqa_train(q[..., :96].contiguous(), k[..., :96].contiguous(), v[..., :96].contiguous())
     with pytest.raises(NotImplementedError):
         gfa.flash_attn_gqa_train(q.float(), k.float(), v.float())
 
