@@ -548,7 +548,7 @@ def run_single(args, wl, world, rank, local):
     torch.cuda.empty_cache()
 
     # the other configurations of the reference's sweep, through the same API
-    sweep, cfg4 = None, None
+    sweep, cfg4, cfg5 = None, None, None
     if world == 1 and not args.no_sweep and args.workload == "cfg2" and args.seqlen is None:
         sweep = []
         variants = [("cfg2", dict(N=1024), 20), ("cfg2", dict(N=4096), 5), ("cfg2", dict(N=32768), 2),
@@ -560,6 +560,7 @@ def run_single(args, wl, world, rank, local):
             r["workload"] = name
             sweep.append(r)
         cfg4 = run_cfg4_one_gpu(device, stream, steps=3)
+        cfg5 = run_decoder_once(device, stream, steps=2)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -581,6 +582,7 @@ def run_single(args, wl, world, rank, local):
             gpu_launches=(1 + len(names)) * args.steps, kernel_status=status,
             bwd_path="materialised (workspace %d bytes)" % ws_bytes if len(names) == 2 else "recompute",
             peak_mem_gb=round(peak_gb, 3), recompute_bwd=recompute, sweep=sweep, cfg4_1gpu=cfg4,
+            cfg5_decoder_1gpu=cfg5,
         )
         print(json.dumps(line), flush=True)
 
@@ -746,6 +748,33 @@ def run_strong(args, wl, world, rank, local):
                               "(plus 5 NCCL all-gathers, not counted)",
         )
         print(json.dumps(line), flush=True)
+
+
+def run_decoder_once(device, stream, steps=2, warmup=1):
+    """Config 5 on one GPU: forward tokens/s of the synthetic 35-layer decoder
+    with every attention layer through hf_integration (one N=16384 sequence)."""
+    from gemma_triton_flash_attn import register_triton_attention
+    from gemma_triton_flash_attn.gemma4_synthetic import Gemma4SyntheticConfig, Gemma4SyntheticDecoder
+
+    register_triton_attention()
+    cfg = Gemma4SyntheticConfig()
+    model = Gemma4SyntheticDecoder(cfg).to(device=device, dtype=torch.bfloat16).init_weights(seed=0)
+    N = WORKLOADS["cfg5"]["N"]
+    g = torch.Generator().manual_seed(1000)
+    ids = torch.randint(0, cfg.vocab_size, (1, N), generator=g).to(device)
+
+    def step():
+        with torch.no_grad():
+            model(ids)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    ms = time_loop(step, steps, stream)
+    del model
+    torch.cuda.empty_cache()
+    return dict(value=round(N / (ms * 1e-3), 1), unit="tokens/s", ms_per_step=round(ms, 3),
+                workload=WORKLOADS["cfg5"]["name"])
 
 
 def run_decoder(args, wl, world, rank, local):
