@@ -136,17 +136,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       // P / dS blocks are read once (evict-first); Q and dO tiles are read by
       // every key tile of the group (evict-last).
       const uint64_t pol_ws = l2_policy_evict_first(), pol_qdo = l2_policy_evict_last();
-      const long long before_lo = ws_blocks_before(t_lo, N, p.causal, p.window);
-      for (int g0 = 0; g0 < G && ok; ++g0) {
-        const int hq = h * G + g0;
-        const long long head0 = (static_cast<long long>(b) * p.Hq + hq) * p.ws_bph;
-        long long before = before_lo;
-        for (int t = t_lo; t < t_hi && ok; ++t) {
-          int jlo, jn;
-          ws_key_blocks(t, N, p.causal, p.window, jlo, jn);
-          const long long blk = head0 + before + (kblk - jlo);
-          before += jn;
-          if (!(kblk >= jlo && kblk < jlo + jn)) continue;
+      // Sub-items in the order (query tile t descending, query head g0): all
+      // pairs of a KV group start at the last query tile and walk down
+      // together, so concurrent pairs read the same Q / dO tiles from L2.
+      long long before = ws_blocks_before(t_hi, N, p.causal, p.window);  // blocks of tiles < t_hi
+      for (int t = t_hi - 1; t >= t_lo && ok; --t) {
+        int jlo, jn;
+        ws_key_blocks(t, N, p.causal, p.window, jlo, jn);
+        before -= jn;  // now: blocks of tiles < t
+        if (!(kblk >= jlo && kblk < jlo + jn)) continue;
+        for (int g0 = 0; g0 < G && ok; ++g0) {
+          const int hq = h * G + g0;
+          const long long blk = (static_cast<long long>(b) * p.Hq + hq) * p.ws_bph + before + (kblk - jlo);
           int st;
           // [dS^T | P^T]: 128 queries x this CTA's 64 keys of the block, each
           ok = acquire(st);
@@ -181,9 +182,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         return mbar_wait_cluster(BAR_FULL(c % NST), (c / NST) & 1u, abort_flag, p.status, ST_TIMEOUT_RING_FULL, p.wait_limit);
       };
       auto sdesc = [&](uint32_t c) { return dRing + static_cast<uint64_t>(((c % NST) * C::STAGE_BYTES) >> 4); };
-      for (int g0 = 0; g0 < G && ok; ++g0) {
-        for (int t = t_lo; t < t_hi && ok; ++t) {
-          if (!stored(t)) continue;
+      for (int t = t_hi - 1; t >= t_lo && ok; --t) {
+        if (!stored(t)) continue;
+        for (int g0 = 0; g0 < G && ok; ++g0) {
           const uint32_t cA = cnt;  // [dS^T | P^T]
           ok = full(cA);
           if (!ok) break;
