@@ -548,7 +548,7 @@ def run_single(args, wl, world, rank, local):
     torch.cuda.empty_cache()
 
     # the other configurations of the reference's sweep, through the same API
-    sweep, cfg4, cfg5 = None, None, None
+    sweep, cfg4, cfg5, host = None, None, None, None
     if world == 1 and not args.no_sweep and args.workload == "cfg2" and args.seqlen is None:
         sweep = []
         variants = [("cfg2", dict(N=1024), 20), ("cfg2", dict(N=4096), 5), ("cfg2", dict(N=32768), 2),
@@ -560,6 +560,7 @@ def run_single(args, wl, world, rank, local):
             r["workload"] = name
             sweep.append(r)
         cfg4 = run_cfg4_one_gpu(device, stream, steps=3)
+        host = host_overhead(device, stream)
         cfg5 = run_decoder_once(device, stream, steps=2)
 
     cpu = None
@@ -582,9 +583,32 @@ def run_single(args, wl, world, rank, local):
             gpu_launches=(1 + len(names)) * args.steps, kernel_status=status,
             bwd_path="materialised (workspace %d bytes)" % ws_bytes if len(names) == 2 else "recompute",
             peak_mem_gb=round(peak_gb, 3), recompute_bwd=recompute, sweep=sweep, cfg4_1gpu=cfg4,
-            cfg5_decoder_1gpu=cfg5,
+            cfg5_decoder_1gpu=cfg5, host_overhead=host,
         )
         print(json.dumps(line), flush=True)
+
+
+def host_overhead(device, stream, n=1024, calls=30):
+    """Host (CPU) cost of one fwd+bwd through the public autograd API at a short
+    sequence, where the GPU work per call is smallest: wall time per call of
+    a loop that only enqueues (the GPU queue absorbs the launches), against
+    the GPU time per call from CUDA events."""
+    wl = dict(WORKLOADS["cfg2"])
+    wl["N"] = n
+    q, k, v, do = make_inputs(wl, 7, device)
+    step = train_step_fn(q, k, v, do, True, 0)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(calls):
+        step()
+    host_ms = (time.perf_counter() - t0) * 1e3 / calls
+    torch.cuda.synchronize()
+    gpu_ms = time_loop(step, calls, stream)
+    return dict(N=n, host_ms_per_call=round(host_ms, 4), gpu_ms_per_call=round(gpu_ms, 4),
+                note="config-2 shape at N=1024; host = enqueue-only wall time per public-API fwd+bwd "
+                     "(ctypes, tensor-map encoding, autograd, allocations); 3 kernels per call")
 
 
 def run_cfg4_one_gpu(device, stream, steps=3, warmup=2):

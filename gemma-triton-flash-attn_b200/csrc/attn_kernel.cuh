@@ -13,29 +13,30 @@
 //              flash_attn/attention.py:1079-1213 (packed GQA: one program per KV
 //              block loops over every Q head of its group, no atomics)
 //
+// This 1-CTA template runs head_dim 64, 128 and 256 (the whole fp32
+// accumulator of a 128-row tile plus the score buffers fit one SM's 512 TMEM
+// columns); head_dim 512 runs on CTA pairs (attn_pair_kernel.cuh).
+//
 // Structure of one CTA (256 threads):
 //   warp 0      TMA producer: loads the resident row tile (R1, R2) once, then
 //               streams 64-column panels of the column operands through a ring.
 //   warp 1      allocates TMEM and issues every tcgen05.mma from one thread.
-//   warps 4..7  "row" warps: read scores from TMEM, apply mask / softmax /
-//               gradient algebra, write P or dS (16-bit) back to TMEM (M=128)
-//               or to shared memory (M=64), run the epilogue.
+//   warps 4..7  "row" warps (warp w reads TMEM lane quadrant w % 4): read
+//               scores from TMEM, apply mask / softmax / gradient algebra,
+//               write P or dS (16-bit) back into the score columns, run the
+//               epilogue.
 //
-// A "row tile" is M rows that stay resident (Q rows for FWD/DQ, K rows for
+// A "row tile" is 128 rows that stay resident (Q rows for FWD/DQ, K rows for
 // DK/DV). The kernel loops over "items": column blocks of BN rows of the other
 // operand (KV blocks for FWD/DQ; (query head, Q block) pairs for DK/DV).
 // Per item:
 //   scores  S  = R1 . C1^T              (K-major x K-major, contraction over D)
 //           dP = R2 . C2^T              (DQ / DK only)
-//   acc    += X . Y                     (X = P or dS from TMEM or smem, Y streamed
+//   acc    += X . Y                     (X = P or dS read from TMEM, Y streamed
 //                                        MN-major, contraction over BN)
 //
-// Tensor-memory layout:
-//   M = 128: accumulator chunk in columns [0, DC); score buffers after it.
-//   M =  64: the 64-row MMA shape occupies 16 lanes of each 32-lane quadrant.
-//            The accumulator sits in the lower half-quadrants (lanes 0-15,
-//            32-47, ...) over all 512 columns, the score buffers in the upper
-//            half-quadrants (lane offset 16). This is how head_dim 512 fits.
+// Tensor-memory layout: the accumulator in columns [0, D), the score buffers
+// (S, and dP for DQ / DK) after it; lane = row of the tile.
 #pragma once
 #include "ptx_sm100.cuh"
 
@@ -124,44 +125,37 @@ __host__ __device__ inline long long ws_blocks_before(int t, int N, int causal, 
   return n;
 }
 
-template <int ROLE_, int M_, int D_, int DC_, int BN_, int NS_, int NSTAGES_, int YGROUP_, bool BF16_>
+template <int ROLE_, int D_, int BN_, int NS_, int NSTAGES_, int YGROUP_, bool BF16_>
 struct Cfg {
-  static constexpr int ROLE = ROLE_, M = M_, D = D_, DC = DC_, BN = BN_, NS = NS_;
+  static constexpr int ROLE = ROLE_, M = 128, D = D_, BN = BN_, NS = NS_;
   static constexpr int NSTAGES = NSTAGES_, YGROUP = YGROUP_;
   static constexpr bool BF16 = BF16_;
   static constexpr bool PAIR = false;
   static constexpr int MP = M;  // rows of one grid tile
   static constexpr bool HAS_DP = (ROLE == ROLE_DQ || ROLE == ROLE_DK);
   static constexpr bool ROWS_ARE_Q = (ROLE == ROLE_FWD || ROLE == ROLE_DQ);
-  static constexpr bool ATMEM = (M == 128);  // P / dS handed to the MMA through TMEM
-  static constexpr int NCHUNK = D / DC;
+  static constexpr int NCHUNK = 1;
   static constexpr int PANELS_D = D / 64;
-  static constexpr int PANELS_Y = DC / 64;
+  static constexpr int PANELS_Y = D / 64;
   static constexpr int R_PANEL = M * 128;
   static constexpr int STAGE_BYTES = BN * 128;
   static constexpr int C_BOX = BN, Y_BOX = BN;  // TMA box rows of the streamed operands
   static constexpr int R_BYTES = PANELS_D * R_PANEL * (HAS_DP ? 2 : 1);
   static constexpr int RING_BYTES = NSTAGES * STAGE_BYTES;
-  static constexpr int PBUF_ONE = M * BN * 2;
-  static constexpr int PBUF_BYTES = ATMEM ? 0 : NS * PBUF_ONE;
   static constexpr int NBARS = 2 * NSTAGES + 1 + 2 * NS + 2;
   static constexpr int MISC_BYTES = M * 4 + NBARS * 8 + 16;
-  static constexpr int SMEM_BYTES = 1024 + R_BYTES + RING_BYTES + PBUF_BYTES + MISC_BYTES;
-  // TMEM columns
-  static constexpr int HI = (M == 64) ? 16 : 0;  // lane offset of the score buffers
-  static constexpr int S_COL0 = (M == 128) ? DC : 0;
+  static constexpr int SMEM_BYTES = 1024 + R_BYTES + RING_BYTES + MISC_BYTES;
+  // TMEM columns: accumulator [0, D), score buffers from S_COL0
+  static constexpr int S_COL0 = D;
   static constexpr int SCORE_COLS = NS * BN * (HAS_DP ? 2 : 1);
   static constexpr uint32_t IDESC_S = make_idesc(M, BN, BF16, false);
   static constexpr uint32_t IDESC_Y = make_idesc(M, 64 * YGROUP, BF16, true);
 
-  static_assert(M == 64 || M == 128, "M");
-  static_assert(D % 64 == 0 && DC % 64 == 0 && D % DC == 0, "D");
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
-  static_assert(M == 128 ? (DC + SCORE_COLS <= 512) : (DC <= 512 && SCORE_COLS <= 512), "TMEM");
-  static_assert(PANELS_D % YGROUP == 0 && PANELS_Y % YGROUP == 0 && NSTAGES % YGROUP == 0, "ring groups");
+  static_assert(D % 64 == 0 && D <= 256, "D");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256 && BN % 16 == 0, "BN");
+  static_assert(D + SCORE_COLS <= 512, "TMEM");
+  static_assert(PANELS_D % YGROUP == 0 && NSTAGES % YGROUP == 0, "ring groups");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
-  static_assert(ROLE != ROLE_FWD || M == 128, "forward uses 128-row tiles");
-  static_assert(M == 128 ? (BN % 16 == 0) : (BN % 8 == 0), "N shape");
 };
 
 // The columns a row attends form one interval [lo, hi) of absolute indices:
@@ -258,8 +252,7 @@ __global__ void __launch_bounds__(256, 1)
   uint8_t* sR1 = smem;
   uint8_t* sR2 = smem + C::PANELS_D * C::R_PANEL;
   uint8_t* sRing = smem + C::R_BYTES;
-  uint8_t* sP = sRing + C::RING_BYTES;
-  float* sRow = reinterpret_cast<float*>(sP + C::PBUF_BYTES);
+  float* sRow = reinterpret_cast<float*>(sRing + C::RING_BYTES);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + M);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -285,8 +278,6 @@ __global__ void __launch_bounds__(256, 1)
   idx /= heads;
   const int b = idx % p.B;
   idx /= p.B;
-  const int chunk = idx % C::NCHUNK;
-  idx /= C::NCHUNK;
   // FWD/DQ: the last q tiles carry the most causal work, launch them first.
   const int tile = p.tile_begin + (C::ROWS_ARE_Q ? (p.num_row_tiles - 1 - idx) : idx);
   const int r0 = tile * M;
@@ -377,7 +368,7 @@ __global__ void __launch_bounds__(256, 1)
       auto load_y = [&](int i) -> bool {
         const int c0 = item_col0(i), hc = item_headC(i);
         for (int pn = 0; pn < C::PANELS_Y; ++pn)
-          if (!load_panel(&tmY, 64 * (chunk * C::PANELS_Y + pn), c0, hc)) return false;
+          if (!load_panel(&tmY, 64 * pn, c0, hc)) return false;
         return true;
       };
       for (int s = 0; s < NS && s < n_items && ok; ++s) ok = load_scores(s);
@@ -391,7 +382,7 @@ __global__ void __launch_bounds__(256, 1)
     if (lane == 0) {
       bool ok = mbar_wait(BAR_RFULL, 0, abort_flag, p.status, ST_TIMEOUT_RESIDENT, p.wait_limit);
       tc_fence_after();
-      const uint32_t aR1 = smem_u32(sR1), aR2 = smem_u32(sR2), aRing = smem_u32(sRing), aP = smem_u32(sP);
+      const uint32_t aR1 = smem_u32(sR1), aR2 = smem_u32(sR2), aRing = smem_u32(sRing);
       uint32_t cnt = 0;
       auto scores_from = [&](uint32_t aR, uint32_t d_tmem) -> bool {
         for (int pn = 0; pn < C::PANELS_D; ++pn) {
@@ -412,9 +403,9 @@ __global__ void __launch_bounds__(256, 1)
       };
       auto issue_scores = [&](int i) -> bool {
         const int sb = i % NS;
-        if (!scores_from(aR1, tbase + (C::HI << 16) + C::S_COL0 + sb * BN)) return false;
+        if (!scores_from(aR1, tbase + C::S_COL0 + sb * BN)) return false;
         if constexpr (C::HAS_DP) {
-          if (!scores_from(aR2, tbase + (C::HI << 16) + C::S_COL0 + (NS + sb) * BN)) return false;
+          if (!scores_from(aR2, tbase + C::S_COL0 + (NS + sb) * BN)) return false;
         }
         mma_commit(BAR_SFULL(sb));
         return true;
@@ -436,13 +427,7 @@ __global__ void __launch_bounds__(256, 1)
             const uint64_t bd = sw128_desc(aRing + st0 * C::STAGE_BYTES + t * 2048, C::STAGE_BYTES, 1024);
             const uint32_t d_tmem = tbase + g * 64 * C::YGROUP;
             const uint32_t accum = (i > 0 || t > 0) ? 1u : 0u;
-            if constexpr (C::ATMEM) {
-              mma_ts(d_tmem, tbase + C::S_COL0 + sb * BN + t * 8, bd, C::IDESC_Y, accum);
-            } else {
-              const uint64_t ad =
-                  sw128_desc(aP + sb * C::PBUF_ONE + (t / 4) * (M * 128) + (t % 4) * 32, 16, 1024);
-              mma_ss(d_tmem, ad, bd, C::IDESC_Y, accum);
-            }
+            mma_ts(d_tmem, tbase + C::S_COL0 + sb * BN + t * 8, bd, C::IDESC_Y, accum);
           }
         }
         mma_commit(BAR_ACC);
@@ -462,10 +447,7 @@ __global__ void __launch_bounds__(256, 1)
     const int q4 = warp & 3;  // TMEM lane quadrant this warp may access
     const uint32_t tq = tbase + (static_cast<uint32_t>(q4 * 32) << 16);
     // Row owned by this thread in the score buffers and in the accumulator.
-    const int srow = (M == 128) ? (q4 * 32 + lane) : (q4 * 16 + lane - 16);
-    const int erow = (M == 128) ? (q4 * 32 + lane) : (q4 * 16 + lane);
-    const bool s_active = (M == 128) || lane >= 16;
-    const bool e_active = (M == 128) || lane < 16;
+    const int srow = q4 * 32 + lane;  // row of the tile this thread owns (= its TMEM lane)
     const float LOG2E = 1.4426950408889634f;
     const float sl2 = p.scale_log2;
     bool ok = true;
@@ -491,10 +473,8 @@ __global__ void __launch_bounds__(256, 1)
         }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (s_active) {
-        row_delta = sRow[srow];
-        row_lse2 = (r0 + srow < N) ? p.lse[rowbase_q + r0 + srow] * LOG2E : 0.f;
-      }
+      row_delta = sRow[srow];
+      row_lse2 = (r0 + srow < N) ? p.lse[rowbase_q + r0 + srow] * LOG2E : 0.f;
     }
 
     for (int i = 0; i < n_items && ok; ++i) {
@@ -568,7 +548,7 @@ __global__ void __launch_bounds__(256, 1)
           if (!ok) break;
           tc_fence_after();
 #pragma unroll 1
-          for (int k = 0; k < C::DC / 32; ++k) {
+          for (int k = 0; k < C::D / 32; ++k) {
             uint32_t r[32];
             tmem_ld32(tq + 32 * k, r);
 #pragma unroll
@@ -627,35 +607,16 @@ __global__ void __launch_bounds__(256, 1)
               v[j] = pv;
             }
           }
-          if constexpr (C::ATMEM) {
-            uint32_t w[16];
+          // P / dS as 16-bit pairs over the first half of this chunk's
+          // score columns (the MMA reads A from TMEM)
+          uint32_t w[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) w[j] = pack2<C::BF16>(v[2 * j], v[2 * j + 1]);
-            tmem_st16(tq + s_col + 16 * k, w);
-          } else {
-            if (s_active) {
-              // K-major SWIZZLE_128B tile: 64-column panels, 128-byte rows.
-              uint8_t* prow = sP + sb * C::PBUF_ONE + ((32 * k) / 64) * (M * 128) + srow * 128;
-#pragma unroll
-              for (int cc = 0; cc < 4; ++cc) {
-                const int chunk16 = ((32 * k) % 64) / 8 + cc;
-                uint4 w;
-                w.x = pack2<C::BF16>(v[8 * cc + 0], v[8 * cc + 1]);
-                w.y = pack2<C::BF16>(v[8 * cc + 2], v[8 * cc + 3]);
-                w.z = pack2<C::BF16>(v[8 * cc + 4], v[8 * cc + 5]);
-                w.w = pack2<C::BF16>(v[8 * cc + 6], v[8 * cc + 7]);
-                *reinterpret_cast<uint4*>(prow + ((chunk16 ^ (srow & 7)) * 16)) = w;
-              }
-            }
-          }
+          for (int j = 0; j < 16; ++j) w[j] = pack2<C::BF16>(v[2 * j], v[2 * j + 1]);
+          tmem_st16(tq + s_col + 16 * k, w);
         }
       }
-      if constexpr (C::ATMEM) {
-        tmem_st_wait();
-        tc_fence_before();
-      } else {
-        fence_proxy_async_smem();
-      }
+      tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR_PREADY(sb));
     }
@@ -675,20 +636,20 @@ __global__ void __launch_bounds__(256, 1)
       } else {
         mul = p.scale;
       }
-      const int orow = r0 + erow;
+      const int orow = r0 + srow;
       const long long obase = static_cast<long long>(b) * p.out_sb + static_cast<long long>(h) * p.out_sh +
-                              static_cast<long long>(orow) * p.out_sn + chunk * C::DC;
+                              static_cast<long long>(orow) * p.out_sn;
 #pragma unroll 1
-      for (int k = 0; k < C::DC / 32; ++k) {
+      for (int k = 0; k < C::D / 32; ++k) {
         uint32_t r[32];
         tmem_ld32(tq + 32 * k, r);
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * mul;
-        if (e_active && orow < N) store_row32<C::BF16>(p.out, obase + 32 * k, v);
+        if (orow < N) store_row32<C::BF16>(p.out, obase + 32 * k, v);
       }
       if constexpr (C::ROLE == ROLE_FWD) {
-        if (p.lse != nullptr && chunk == 0 && orow < N) {
+        if (p.lse != nullptr && orow < N) {
           const float LN2 = 0.6931471805599453f;
           p.lse[rowbase_q + orow] = (l_run > 0.f) ? (m_run + __log2f(l_run)) * LN2 : -INFINITY;
         }

@@ -182,21 +182,21 @@ int launch(const CUtensorMap (&maps)[6], KParams p, cudaStream_t stream) {
   return GQAFA_OK;
 }
 
-// Fixed configurations. Cfg<ROLE, M, D, DC, BN, NS, NSTAGES, YGROUP, BF16>
-template <bool BF16> using Fwd256 = Cfg<ROLE_FWD, 128, 256, 256, 128, 2, 8, 4, BF16>;
-template <bool BF16> using Dq256 = Cfg<ROLE_DQ, 128, 256, 256, 128, 1, 6, 2, BF16>;
+// Fixed configurations. Cfg<ROLE, D, BN, NS, NSTAGES, YGROUP, BF16> (128-row tiles)
+template <bool BF16> using Fwd256 = Cfg<ROLE_FWD, 256, 128, 2, 8, 4, BF16>;
+template <bool BF16> using Dq256 = Cfg<ROLE_DQ, 256, 128, 1, 6, 2, BF16>;
 template <bool BF16> using Dk256 = PairCfg<ROLE_DK, 256, 128, 2, 4, BF16>;  // pair: faster than 1-CTA here
-template <bool BF16> using Dv256 = Cfg<ROLE_DV, 128, 256, 256, 128, 2, 8, 4, BF16>;
+template <bool BF16> using Dv256 = Cfg<ROLE_DV, 256, 128, 2, 8, 4, BF16>;
 // head_dim 64 and 128: the 1-CTA template throughout (the whole accumulator
 // and double-buffered scores fit one SM's TMEM); the backward recomputes.
-template <bool BF16> using Fwd128 = Cfg<ROLE_FWD, 128, 128, 128, 128, 2, 8, 2, BF16>;
-template <bool BF16> using Dq128 = Cfg<ROLE_DQ, 128, 128, 128, 128, 1, 8, 2, BF16>;
-template <bool BF16> using Dk128 = Cfg<ROLE_DK, 128, 128, 128, 128, 1, 8, 2, BF16>;
-template <bool BF16> using Dv128 = Cfg<ROLE_DV, 128, 128, 128, 128, 2, 8, 2, BF16>;
-template <bool BF16> using Fwd64 = Cfg<ROLE_FWD, 128, 64, 64, 128, 2, 8, 1, BF16>;
-template <bool BF16> using Dq64 = Cfg<ROLE_DQ, 128, 64, 64, 128, 1, 8, 1, BF16>;
-template <bool BF16> using Dk64 = Cfg<ROLE_DK, 128, 64, 64, 128, 1, 8, 1, BF16>;
-template <bool BF16> using Dv64 = Cfg<ROLE_DV, 128, 64, 64, 128, 2, 8, 1, BF16>;
+template <bool BF16> using Fwd128 = Cfg<ROLE_FWD, 128, 128, 2, 8, 2, BF16>;
+template <bool BF16> using Dq128 = Cfg<ROLE_DQ, 128, 128, 1, 8, 2, BF16>;
+template <bool BF16> using Dk128 = Cfg<ROLE_DK, 128, 128, 1, 8, 2, BF16>;
+template <bool BF16> using Dv128 = Cfg<ROLE_DV, 128, 128, 2, 8, 2, BF16>;
+template <bool BF16> using Fwd64 = Cfg<ROLE_FWD, 64, 128, 2, 8, 1, BF16>;
+template <bool BF16> using Dq64 = Cfg<ROLE_DQ, 64, 128, 1, 8, 1, BF16>;
+template <bool BF16> using Dk64 = Cfg<ROLE_DK, 64, 128, 1, 8, 1, BF16>;
+template <bool BF16> using Dv64 = Cfg<ROLE_DV, 64, 128, 2, 8, 1, BF16>;
 // head_dim 512: CTA pairs, PairCfg<ROLE, D, BN, NS, NSTAGES, BF16>. The forward keeps all 512 O
 // columns in TMEM (256 per CTA), so S is computed once per item. 256-column items make
 // every score MMA an N=256 pair instruction (full tensor rate; N=128 pair MMAs run at 70%), at the

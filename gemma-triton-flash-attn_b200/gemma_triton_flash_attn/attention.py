@@ -222,7 +222,9 @@ def _workspace_limit(device=None):
     driver plus what torch's caching allocator holds unused. A workspace over
     the budget makes the backward run over groups of KV heads (each group's
     share within the budget), and the recomputing backward (no workspace) when
-    one KV head's share is over it too."""
+    one KV head's share is over it too. A workspace that the caching allocator
+    can serve from memory it already holds unused is always allowed (it adds
+    nothing to the process's footprint)."""
     env = os.environ.get("GQAFA_BWD_WORKSPACE_LIMIT")
     if env is not None:
         return int(env)
@@ -243,9 +245,18 @@ def bwd_workspace_size(b, h_q, h_kv, n, d, causal, window):
 
 
 def _alloc_workspace(size, device):
-    limit = _workspace_limit(device)
-    if size <= 0 or (limit is not None and size > limit):
+    if size <= 0:
         return None
+    env = os.environ.get("GQAFA_BWD_WORKSPACE_LIMIT")
+    if env is not None:
+        if size > int(env):
+            return None
+    elif size > torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device):
+        # Memory the caching allocator already holds unused (the previous
+        # step's workspace, typically) is always usable; only new device
+        # memory is held to the budget (which costs a driver query).
+        if size > _workspace_limit(device):
+            return None
     try:
         return torch.empty(size, dtype=torch.uint8, device=device)
     except torch.cuda.OutOfMemoryError:
