@@ -608,7 +608,7 @@ def host_overhead(device, stream, n=1024, calls=30):
     gpu_ms = time_loop(step, calls, stream)
     return dict(N=n, host_ms_per_call=round(host_ms, 4), gpu_ms_per_call=round(gpu_ms, 4),
                 note="config-2 shape at N=1024; host = enqueue-only wall time per public-API fwd+bwd "
-                     "(ctypes, tensor-map encoding, autograd, allocations); 3 kernels per call")
+                     "(autograd, torch operators over the C ABI, tensor-map encoding, allocations); 3 kernels per call")
 
 
 def run_cfg4_one_gpu(device, stream, steps=3, warmup=2):

@@ -1,8 +1,12 @@
-"""ctypes binding of the C ABI in include/gqa_fa_b200.h.
+"""Bindings of the C ABI in include/gqa_fa_b200.h.
 
-The shared library ``libgqa_fa_b200.so`` is built in-tree (``make`` in the
-package directory, or ``__graft_entry__.build()``). There is no CPU or Triton
-fallback: if the library is missing, importing the kernels raises.
+Two in-tree libraries (``make`` in the package directory, or
+``__graft_entry__.build()``): ``libgqa_fa_b200.so``, the kernels behind the C
+ABI, bound here with ctypes for every entry point; and ``libgqa_fa_ops.so``,
+torch operators ``torch.ops.gqafa.fwd`` / ``torch.ops.gqafa.bwd`` over the
+same ABI, which the autograd function's hot path calls (no per-call Python
+argument marshalling). There is no CPU or Triton fallback: if a library is
+missing, loading it raises.
 """
 from __future__ import annotations
 
@@ -42,8 +46,11 @@ EXPORTED_SYMBOLS = (
     "gqafa_set_test_waits",
 )
 
+OPS_PATH = os.path.join(os.path.dirname(LIB_PATH), "libgqa_fa_ops.so")
+
 _lock = threading.Lock()
 _lib = None
+_ops = None
 
 _P = ctypes.c_void_p
 _S = ctypes.POINTER(ctypes.c_longlong)
@@ -109,6 +116,23 @@ def load():
         lib.gqafa_version.restype = ctypes.c_char_p
         _lib = lib
         return lib
+
+
+def ops():
+    """torch.ops.gqafa, loading libgqa_fa_ops.so on first use."""
+    global _ops
+    with _lock:
+        if _ops is None:
+            if not os.path.exists(OPS_PATH):
+                raise ImportError(
+                    f"gemma_triton_flash_attn: torch operator library not found at {OPS_PATH}. "
+                    "Build it with `make -C gemma-triton-flash-attn_b200`. There is no CPU fallback."
+                )
+            import torch
+
+            torch.ops.load_library(OPS_PATH)
+            _ops = torch.ops.gqafa
+    return _ops
 
 
 def strides_arg(strides):

@@ -183,6 +183,10 @@ def _fwd(q, k, v, causal, window, scale, want_lse, rows=None, out=None):
     lib = _lib.load()
     b, h_q, n, d = q.shape
     h_kv, nk = k.shape[1], k.shape[2]
+    if out is None and rows is None:
+        # the hot path: one torch operator call (torch_ops.cpp) over the C ABI
+        o, lse = _lib.ops().fwd(q, k, v, bool(causal), int(window), float(scale), bool(want_lse))
+        return o, (lse if want_lse else None)
     q, k, v = _abi_ready(q), _abi_ready(k), _abi_ready(v)
     if out is None:
         o = torch.empty_like(q)  # keeps q's layout (e.g. HF's (B, N, H, D) storage)
@@ -279,6 +283,17 @@ def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=
     lib = _lib.load()
     b, h_q, n, d = q.shape
     h_kv = k.shape[1]
+    ws = workspace
+    chunks = None
+    if ws is None and stage is None and rows is None:
+        size = bwd_workspace_size(b, h_q, h_kv, n, d, causal, window)
+        ws = _alloc_workspace(size, q.device)
+        if ws is None and size > 0:
+            chunks, ws = _workspace_chunks(size, b, h_kv, q.device)
+    if out is None and stage is None and rows is None and chunks is None:
+        # the hot path: one torch operator call (torch_ops.cpp) over the C ABI;
+        # gqafa_bwd_ws with a workspace, the recomputing gqafa_bwd without
+        return _lib.ops().bwd(q, k, v, o, lse, do, bool(causal), int(window), float(scale), ws)
     q, k, v, o = _abi_ready(q), _abi_ready(k), _abi_ready(v), _abi_ready(o)
     do = _abi_ready(do)
     if out is None:
@@ -293,13 +308,6 @@ def _bwd(q, k, v, o, lse, do, causal, window, scale, stage=None, out=None, rows=
         lse = lse.contiguous()
     if not delta.is_contiguous():
         raise ValueError("delta must be a contiguous (B, H_Q, N) float32 tensor")
-    ws = workspace
-    chunks = None
-    if ws is None and stage is None and rows is None:
-        size = bwd_workspace_size(b, h_q, h_kv, n, d, causal, window)
-        ws = _alloc_workspace(size, q.device)
-        if ws is None and size > 0:
-            chunks, ws = _workspace_chunks(size, b, h_kv, q.device)
     if ws is not None:
         tail = (ws.data_ptr(), ws.numel() * ws.element_size())
         if stage is None:

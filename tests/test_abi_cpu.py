@@ -116,3 +116,18 @@ def test_bwd_workspace_size(n, causal, window):
     assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 128, int(causal), window) == 0  # recomputing backward
     assert lib.gqafa_bwd_workspace_size(2, 8, 2, n, 96, int(causal), window) == -1
     assert lib.gqafa_bwd_workspace_size(2, 8, 3, n, 512, int(causal), window) == -1
+
+
+def test_torch_operators_load_and_propagate_shapes():
+    """libgqa_fa_ops.so registers torch.ops.gqafa.fwd / bwd over the C ABI;
+    their Meta kernels give the output shapes without a GPU."""
+    import torch
+
+    ops = _lib.ops()
+    q = torch.empty(2, 8, 100, 512, device="meta", dtype=torch.bfloat16)
+    k = torch.empty(2, 2, 100, 512, device="meta", dtype=torch.bfloat16)
+    o, lse = ops.fwd(q, k, k, True, 0, 512 ** -0.5, True)
+    assert o.shape == q.shape and o.dtype == q.dtype and lse.shape == (2, 8, 100) and lse.dtype == torch.float32
+    dq, dk, dv = ops.bwd(q, k, k, o, lse, q, True, 0, 512 ** -0.5, None)
+    assert dq.shape == q.shape and dk.shape == k.shape and dv.shape == k.shape
+    assert "Tensor? workspace" in str(ops.bwd.default._schema)
