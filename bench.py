@@ -75,6 +75,8 @@ def parse_args():
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="N > 1: strong = one config-4 problem over the GPUs with all-gathers (default); "
                          "weak = config 2 per GPU, no collective")
+    ap.add_argument("--gather", choices=["nccl", "ce"], default="nccl",
+                    help="N > 1 strong scaling: all-gathers by NCCL, or copy-engine pushes into symmetric memory")
     ap.add_argument("--seqlen", type=int, default=None, help="override N (not the headline)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
@@ -647,7 +649,8 @@ def run_strong(args, wl, world, rank, local):
     B, Hq, Hkv, N, D, causal = (wl[x] for x in ("B", "Hq", "Hkv", "N", "D", "causal"))
     window = _window(wl)
     q, k, v, do = make_inputs(wl, 1234, device)  # the same problem on every rank
-    att = UnitShardedAttention(B, Hq, Hkv, N, D, wl["dtype"], device, causal=causal, slide_size=wl["W"])
+    att = UnitShardedAttention(B, Hq, Hkv, N, D, wl["dtype"], device, causal=causal, slide_size=wl["W"],
+                               gather=args.gather)
     step = lambda: att.step(q, k, v, do)  # noqa: E731
     total = attn_flops(B, Hq, N, D, causal, window, bwd=True)
 
@@ -757,12 +760,15 @@ def run_strong(args, wl, world, rank, local):
             config=dict(workload=wl["name"], global_batch=B, H_Q=Hq, H_KV=Hkv, N=N, D=D, causal=causal,
                         seq_len=N, units=B * Hkv, units_per_gpu=B * Hkv // world,
                         parallelism=f"{B * Hkv} (b,kv-group) units in equal blocks over {world} GPUs; "
-                                    "O/LSE/dQ/dK/dV all-gathered (NCCL) inside the step",
+                                    f"O/LSE/dQ/dK/dV all-gathered ({att.gather}) inside the step",
                         l2="inputs larger than L2 (Q, dO 1 GiB each); no flush"),
             collective=dict(ms_compute_only=round(ms_c, 3), exposed_ms=round(ms_max - ms_c, 3),
                             exposed_share=round(max(0.0, ms_max - ms_c) / ms_max, 4),
                             bytes_gathered_per_rank=round(gathered * (world - 1) / world),
-                            op="all_gather_into_tensor x5 (in place), overlapped with the next kernels"),
+                            op=("all_gather_into_tensor x5 (NCCL, in place)" if att.gather == "nccl" else
+                                "copy-engine pushes of each rank's slice into every peer's symmetric buffer x5, "
+                                "one-element NCCL all-reduce to close the step")
+                            + ", overlapped with the next kernels"),
             roofline=dict(bound="tensor", kernel="whole step per rank", achieved=round(per_rank / ms_max / 1e9, 1),
                           peak=peaks["tflops_burst"], unit="TFLOP/s",
                           frac=round(per_rank / ms_max / 1e9 / peaks["tflops_burst"], 4), traffic=None),

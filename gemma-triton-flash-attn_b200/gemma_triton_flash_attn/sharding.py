@@ -188,10 +188,20 @@ class UnitShardedAttention:
     ``fwd_fn(q, k, v, o, lse)`` and ``bwd_fn(stage, q, k, v, o, lse, do, dq,
     dk, dv, delta, workspace)`` replace the kernels (CPU tests); by default
     they are this library's CUDA launches.
+
+    ``gather="ce"`` (GPUs only) replaces the NCCL all-gathers by copy-engine
+    pushes over NVLink: the output buffers are symmetric memory
+    (torch.distributed._symmetric_memory), every rank copies its own slice
+    into the same slice of every peer's buffer with cudaMemcpyAsync on its own
+    copy streams, and ``wait()`` ends with a one-element NCCL all-reduce that
+    orders every rank after all pushes. Copy engines use no SMs, so the
+    gathers take nothing from the kernels they overlap. A step's outputs stay
+    valid until the next ``step`` / ``forward`` on any rank (peers push into
+    them).
     """
 
     def __init__(self, batch, heads_q, heads_kv, seqlen, head_dim, dtype, device, causal=True, slide_size=0,
-                 softmax_scale=None, group=None, fwd_fn=None, bwd_fn=None):
+                 softmax_scale=None, group=None, fwd_fn=None, bwd_fn=None, gather="nccl", copy_streams=4):
         from .attention import _normalize_window
 
         self.group = group
@@ -205,13 +215,29 @@ class UnitShardedAttention:
         self.window = _normalize_window(causal, slide_size, seqlen)
         self.scale = (1.0 / math.sqrt(head_dim)) if softmax_scale is None else float(softmax_scale)
         B, Hq, Hkv, N, D = self.shape
-        kw = dict(dtype=dtype, device=device)
-        self.o = torch.empty((B, Hq, N, D), **kw)
-        self.dq = torch.empty((B, Hq, N, D), **kw)
-        self.dk = torch.empty((B, Hkv, N, D), **kw)
-        self.dv = torch.empty((B, Hkv, N, D), **kw)
-        self.lse = torch.empty((B, Hq, N), dtype=torch.float32, device=device)
+        if gather not in ("nccl", "ce"):
+            raise ValueError(f"gather must be 'nccl' or 'ce', got {gather!r}")
+        self.gather = gather if self.world > 1 else "nccl"
+        alloc = torch.empty
+        if self.gather == "ce":
+            import torch.distributed._symmetric_memory as symm
+
+            alloc = lambda shape, dtype, device: symm.empty(shape, dtype=dtype, device=device)  # noqa: E731
+        self.o = alloc((B, Hq, N, D), dtype=dtype, device=device)
+        self.dq = alloc((B, Hq, N, D), dtype=dtype, device=device)
+        self.dk = alloc((B, Hkv, N, D), dtype=dtype, device=device)
+        self.dv = alloc((B, Hkv, N, D), dtype=dtype, device=device)
+        self.lse = alloc((B, Hq, N), dtype=torch.float32, device=device)
         self.delta = torch.empty((B, Hq, N), dtype=torch.float32, device=device)
+        self._peers = {}
+        if self.gather == "ce":
+            pg = group if group is not None else dist.group.WORLD
+            for name in ("o", "dq", "dk", "dv", "lse"):
+                t = getattr(self, name)
+                hdl = symm.rendezvous(t, pg)
+                self._peers[name] = [hdl.get_buffer(p, tuple(t.shape), t.dtype) for p in range(self.world)]
+            self._copy_streams = [torch.cuda.Stream(device) for _ in range(copy_streams)]
+            self._flag = torch.zeros(1, dtype=torch.int32, device=device)
         self.runs = list(self.plan.runs())
         self._fwd_fn = fwd_fn or self._kernel_fwd
         self._bwd_fn = bwd_fn or self._kernel_bwd
@@ -253,21 +279,35 @@ class UnitShardedAttention:
         b, kv0, kv1 = self.runs[i]
         return t[b:b + 1, kv0:kv1]
 
-    def _gather(self, t):
-        """Start the in-place all-gather of this rank's block of `t` (flattened
-        over batch and heads, which are unit-ordered)."""
+    def _gather(self, t, name=None):
+        """Start the all-gather of this rank's block of `t` (flattened over
+        batch and heads, which are unit-ordered): in place with NCCL, or as
+        copy-engine pushes into the peers' symmetric buffers."""
         if self.world == 1:
             return
         flat = t.view(self.world, -1)
-        self._works.append(dist.all_gather_into_tensor(t.view(-1), flat[self.rank], group=self.group, async_op=True))
+        if self.gather == "nccl":
+            self._works.append(dist.all_gather_into_tensor(t.view(-1), flat[self.rank], group=self.group,
+                                                           async_op=True))
+            return
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream(t.device))
+        mine = flat[self.rank]
+        ns = len(self._copy_streams)
+        for j in range(1, self.world):  # peers in rotated order, spread over the copy streams
+            p = (self.rank + j) % self.world
+            s = self._copy_streams[(j - 1) % ns]
+            s.wait_event(ready)
+            with torch.cuda.stream(s):
+                self._peers[name][p].view(self.world, -1)[self.rank].copy_(mine, non_blocking=True)
 
     # ---- passes --------------------------------------------------------------
     def forward(self, q, k, v):
         """O and LSE of this rank's units, then their all-gather (started, not awaited)."""
         for i in range(len(self.runs)):
             self._fwd_fn(self._qv(i, q), self._kvv(i, k), self._kvv(i, v), self._qv(i, self.o), self._qv(i, self.lse))
-        self._gather(self.o)
-        self._gather(self.lse)
+        self._gather(self.o, "o")
+        self._gather(self.lse, "lse")
         return self.o, self.lse
 
     def backward(self, q, k, v, do):
@@ -281,13 +321,20 @@ class UnitShardedAttention:
                 self._bwd_fn(stage, qv(q), kvv(k), kvv(v), qv(self.o), qv(self.lse), qv(do), qv(self.dq),
                              kvv(self.dk), kvv(self.dv), qv(self.delta), ws)
             if stage == 0:
-                self._gather(self.dq)
-        self._gather(self.dk)
-        self._gather(self.dv)
+                self._gather(self.dq, "dq")
+        self._gather(self.dk, "dk")
+        self._gather(self.dv, "dv")
         return self.dq, self.dk, self.dv
 
     def wait(self):
         """Make the calling stream wait for every collective started so far."""
+        if self.gather == "ce" and self.world > 1:
+            cur = torch.cuda.current_stream(self._flag.device)
+            for s in self._copy_streams:
+                cur.wait_stream(s)
+            # every rank's pushes are complete once every rank has reached this
+            # all-reduce (each enqueues it after its own copies)
+            self._works.append(dist.all_reduce(self._flag, group=self.group, async_op=True))
         for w in self._works:
             w.wait()
         self._works = []

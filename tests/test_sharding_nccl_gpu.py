@@ -37,9 +37,9 @@ def _worker(rank, world, port, out_dir, split=False):
         from gemma_triton_flash_attn import sharding as sh
 
         q, k, v, do = _inputs(f"cuda:{rank}", split in ("seq", "heads"))
-        if split == "persistent":
+        if split in ("persistent", "persistent_ce"):
             att = sh.UnitShardedAttention(q.shape[0], q.shape[1], k.shape[1], q.shape[2], q.shape[3], q.dtype,
-                                          q.device, causal=True)
+                                          q.device, causal=True, gather="ce" if split == "persistent_ce" else "nccl")
             for _ in range(2):  # the second step reuses every buffer
                 o, lse, dq, dk, dv = att.step(q, k, v, do)
             torch.cuda.synchronize()
@@ -56,8 +56,9 @@ def _worker(rank, world, port, out_dir, split=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("split", [False, "persistent", "seq", "heads"],
-                         ids=["units", "unit_sharded_attention", "sequence_split", "head_split"])
+@pytest.mark.parametrize("split", [False, "persistent", "persistent_ce", "seq", "heads"],
+                         ids=["units", "unit_sharded_attention", "unit_sharded_attention_copy_engines",
+                              "sequence_split", "head_split"])
 def test_sharded_equals_single_gpu(tmp_path, split, monkeypatch):
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
