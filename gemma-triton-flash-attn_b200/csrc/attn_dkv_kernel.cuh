@@ -257,7 +257,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = 0.f;
             }
-            if (orow < N) store_row32<C::BF16>(out, obase + 256 * g + 128 * half + 32 * k, v);
+            if (orow < N) store_out32<C::BF16>(out, obase + 256 * g + 128 * half + 32 * k, v, p.out_f32 != 0);
           }
         }
       }

@@ -82,6 +82,9 @@ struct KParams {
   // issue nothing, so every wait of the launch runs into that bound.
   long long wait_limit;
   int no_loads;
+  // dK / dV outputs (out, out2 of the DK, DV and dK+dV roles) are fp32 rather
+  // than the input dtype: partial sums that a caller adds up before rounding.
+  int out_f32;
 };
 
 // Indices of the wait-cycle diagnostics counters.
@@ -225,6 +228,21 @@ __device__ __forceinline__ float row_dot(const uint16_t* a, const uint16_t* b, i
     acc += unpack_hi<BF16>(xw) * unpack_hi<BF16>(yw);
   }
   return acc;
+}
+
+template <bool BF16>
+__device__ __forceinline__ void store_row32(void* base, long long off_elems, const float (&v)[32]);
+
+// 32 values of an output row: 16-bit like the inputs, or fp32 when f32.
+template <bool BF16>
+__device__ __forceinline__ void store_out32(void* base, long long off_elems, const float (&v)[32], bool f32) {
+  if (f32) {
+    float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + off_elems);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+    store_row32<BF16>(base, off_elems, v);
+  }
 }
 
 template <bool BF16>
@@ -646,7 +664,7 @@ __global__ void __launch_bounds__(256, 1)
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * mul;
-        if (orow < N) store_row32<C::BF16>(p.out, obase + 32 * k, v);
+        if (orow < N) store_out32<C::BF16>(p.out, obase + 32 * k, v, !C::ROWS_ARE_Q && p.out_f32);
       }
       if constexpr (C::ROLE == ROLE_FWD) {
         if (p.lse != nullptr && orow < N) {

@@ -803,7 +803,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * mul;
-            if (orow < N) store_row32<C::BF16>(p.out, obase + 256 * g + 128 * half + 32 * k, v);
+            if (orow < N)
+              store_out32<C::BF16>(p.out, obase + 256 * g + 128 * half + 32 * k, v, !C::ROWS_ARE_Q && p.out_f32);
           }
         }
       }

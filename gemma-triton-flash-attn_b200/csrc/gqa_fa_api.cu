@@ -217,6 +217,7 @@ template <bool BF16> using Dkv256 = DkvCfg<256, 7, BF16>;
 struct Problem {
   int B, Hq, Hkv, N, D, causal, window;
   int Nk;  // key length (== N except for the KV-cache forward)
+  bool kv_f32;  // dK / dV written as fp32 (gqafa_bwd_partial)
   int row_begin, row_end;  // rows of the row-tile dimension to compute
   float scale;
   bool bf16;
@@ -242,6 +243,7 @@ int check_problem(int B, int Hq, int Hkv, int N, int D, float scale, int causal,
   pr->D = D;
   pr->causal = causal ? 1 : 0;
   pr->Nk = N;
+  pr->kv_f32 = false;
   // Reference semantics: the window only applies to causal attention and a
   // window covering the whole sequence is plain causal.
   pr->window = (pr->causal && window > 0 && window < N) ? window : 0;
@@ -347,6 +349,7 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
     p.lse = const_cast<float*>(lse);
     p.delta = delta;
     p.status = status;
+    p.out_f32 = pr.kv_f32 ? 1 : 0;
     maps[5] = maps[0];
     if ((rc = launch<CK>(maps, p, st))) return rc;
   }
@@ -362,6 +365,7 @@ int bwd_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, const 
     p.lse = const_cast<float*>(lse);
     p.delta = delta;
     p.status = status;
+    p.out_f32 = pr.kv_f32 ? 1 : 0;
     maps[5] = maps[0];
     if ((rc = launch<CV>(maps, p, st))) return rc;
   }
@@ -447,6 +451,7 @@ int bwd_ws_impl(const Problem& pr, const TensorDesc& q, const TensorDesc& k, con
     p.out2_sb = dvd.sb;
     p.out2_sh = dvd.sh;
     p.out2_sn = dvd.sn;
+    p.out_f32 = pr.kv_f32 ? 1 : 0;
     p.ws = ws;
     p.ws_bph = bph;
     p.ws_blocks = nblk;
@@ -566,13 +571,14 @@ static int bwd_entry(int stages, int row_begin, int row_end, const void* q, cons
                          const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
                          const long long* dv_strides, float* delta, int batch, int heads_q, int heads_kv,
                          int seqlen, int head_dim, float softmax_scale, int causal, int window, int dtype,
-                         void* stream) {
+                         void* stream, bool kv_f32 = false) {
   g_last_error.clear();
   if (stages <= 0 || stages > 7) return fail(GQAFA_ERR_INVALID, "stage mask %d not in 1..7", stages);
   Problem pr{};
   int rc;
   if ((rc = check_problem(batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, window, dtype, &pr)))
     return rc;
+  pr.kv_f32 = kv_f32;
   if (row_end < 0) row_end = seqlen;
   if ((rc = set_rows(&pr, row_begin, row_end))) return rc;
   TensorDesc qd, kd, vd, od, dod, dqd, dkd, dvd;
@@ -649,14 +655,16 @@ extern "C" long long gqafa_bwd_workspace_size(int batch, int heads_q, int heads_
   return ws_bytes(pr);
 }
 
-static int bwd_ws_entry(int stages, GQAFA_BWD_PARAMS, void* workspace, long long workspace_bytes) {
+static int bwd_ws_entry(int stages, GQAFA_BWD_PARAMS, void* workspace, long long workspace_bytes,
+                        bool kv_f32 = false) {
   g_last_error.clear();
   Problem pr{};
   int rc;
   if ((rc = check_problem(batch, heads_q, heads_kv, seqlen, head_dim, softmax_scale, causal, window, dtype, &pr)))
     return rc;
+  pr.kv_f32 = kv_f32;
   const long long need = ws_bytes(pr);
-  if (need == 0) return bwd_entry(stages == 2 ? 6 : (stages == 1 ? 1 : 7), 0, -1, GQAFA_BWD_ARGS);
+  if (need == 0) return bwd_entry(stages == 2 ? 6 : (stages == 1 ? 1 : 7), 0, -1, GQAFA_BWD_ARGS, kv_f32);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(GQAFA_ERR_INVALID, "workspace of %lld bytes needed, got %lld", need, workspace_bytes);
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
@@ -686,6 +694,12 @@ static int bwd_ws_entry(int stages, GQAFA_BWD_PARAMS, void* workspace, long long
 
 extern "C" int gqafa_bwd_ws(GQAFA_BWD_PARAMS, void* workspace, long long workspace_bytes) {
   return bwd_ws_entry(3, GQAFA_BWD_ARGS, workspace, workspace_bytes);
+}
+
+extern "C" int gqafa_bwd_partial(GQAFA_BWD_PARAMS, void* workspace, long long workspace_bytes) {
+  if (workspace != nullptr && workspace_bytes > 0)
+    return bwd_ws_entry(3, GQAFA_BWD_ARGS, workspace, workspace_bytes, true);
+  return bwd_entry(7, 0, -1, GQAFA_BWD_ARGS, true);
 }
 
 extern "C" int gqafa_bwd_ws_stage(int stage, GQAFA_BWD_PARAMS, void* workspace, long long workspace_bytes) {

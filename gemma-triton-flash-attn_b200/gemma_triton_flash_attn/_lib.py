@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "gqafa_bwd_noalloc",
     "gqafa_bwd_ws",
     "gqafa_bwd_ws_stage",
+    "gqafa_bwd_partial",
     "gqafa_bwd_workspace_size",
     "gqafa_fwd_rows",
     "gqafa_bwd_stage_rows",
@@ -100,6 +101,8 @@ def load():
         lib.gqafa_bwd_ws.restype = _I
         lib.gqafa_bwd_ws_stage.argtypes = [_I] + lib.gqafa_bwd.argtypes + [_P, _L]
         lib.gqafa_bwd_ws_stage.restype = _I
+        lib.gqafa_bwd_partial.argtypes = lib.gqafa_bwd.argtypes + [_P, _L]
+        lib.gqafa_bwd_partial.restype = _I
         lib.gqafa_bwd_workspace_size.argtypes = [_I] * 7
         lib.gqafa_bwd_workspace_size.restype = _L
         lib.gqafa_supported.argtypes = [_I, _I]

@@ -530,7 +530,9 @@ def split_backward(q, k, v, o, lse, do, causal=False, slide_size=0, softmax_scal
 # ranks of a unit each take G/s of its query heads over the whole sequence.
 # Forward and dQ need nothing from the other ranks; dK and dV of the unit's KV
 # head are the sum of the s ranks' partial results (each over its G/s heads),
-# the path's one real reduction, done with an all-reduce in fp32. Every kernel
+# the path's one real reduction: the kernels write the partials in fp32
+# (gqafa_bwd_partial) and they are summed by an all-reduce within the unit's
+# ranks before the one rounding to the input dtype. Every kernel
 # keeps its full-sequence grid, unlike the sequence split, whose dK/dV launches
 # shrink to one KV head and a fraction of its rows.
 
@@ -571,27 +573,76 @@ def head_split_forward(q, k, v, causal=False, slide_size=0, softmax_scale=None, 
     return o, lse
 
 
-def head_split_backward(q, k, v, o, lse, do, causal=False, slide_size=0, softmax_scale=None, group=None):
-    """Backward of head_split_forward: dQ per rank, dK/dV summed over the ranks
-    of each unit (fp32 all-reduce); full gradients on every rank."""
-    from .attention import flash_attn_gqa_backward
+_SUBGROUPS = {}
 
+
+def _unit_subgroup(group, units, s, unit):
+    """The process group of the s ranks of `unit` (created once, by every rank
+    for every unit in the same order, as torch.distributed requires)."""
+    granks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
+    key = (tuple(granks), s)
+    if key not in _SUBGROUPS:
+        _SUBGROUPS[key] = [dist.new_group([granks[u * s + j] for j in range(s)]) for u in range(units)]
+    return _SUBGROUPS[key][unit]
+
+
+def _partial_backward(q, k, v, o, lse, do, causal, window, scale):
+    """dQ in the input dtype and dK, dV as fp32 partials (gqafa_bwd_partial:
+    the materialised backward when its workspace fits, else the recomputing
+    one), for a rank that holds some of the query heads of a KV group."""
+    from . import _lib
+    from .attention import _abi_ready, _alloc_workspace, _bwd_args, bwd_workspace_size
+
+    b, h_q, n, d = q.shape
+    h_kv = k.shape[1]
+    q, k, v, o, do = (_abi_ready(t) for t in (q, k, v, o, do))
+    dq = torch.empty_like(q)
+    dk = torch.empty(k.shape, dtype=torch.float32, device=q.device)
+    dv = torch.empty(v.shape, dtype=torch.float32, device=q.device)
+    delta = torch.empty((b, h_q, n), dtype=torch.float32, device=q.device)
+    ws = _alloc_workspace(bwd_workspace_size(b, h_q, h_kv, n, d, causal, window), q.device)
+    tail = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    _lib.check(_lib.load().gqafa_bwd_partial(
+        *_bwd_args(q, k, v, o, do, lse.contiguous(), dq, dk, dv, delta, causal, window, scale, stream), *tail))
+    return dq, dk, dv
+
+
+def head_split_backward(q, k, v, o, lse, do, causal=False, slide_size=0, softmax_scale=None, group=None):
+    """Backward of head_split_forward: dQ per rank; dK/dV of each unit are the
+    sum of its s ranks' fp32 partials (an all-reduce within those s ranks
+    only, before any rounding), then rounded once and all-gathered; full
+    gradients on every rank."""
+    from .attention import _check_inputs, _normalize_window
+
+    _check_inputs(q, k, v)
     B, Hq, N, D = q.shape
     Hkv = k.shape[1]
+    window = _normalize_window(causal, slide_size, N)
+    scale = (1.0 / math.sqrt(D)) if softmax_scale is None else float(softmax_scale)
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     b, kv, h0, nh = head_split_assignment(B, Hq, Hkv, world, rank)
+    units = B * Hkv
+    s = world // units
     hs = slice(h0, h0 + nh)
-    dq_loc, dk_loc, dv_loc = flash_attn_gqa_backward(
+    dq_loc, dk_p, dv_p = _partial_backward(
         q[b:b + 1, hs], k[b:b + 1, kv:kv + 1], v[b:b + 1, kv:kv + 1], o[b:b + 1, hs],
-        lse[b:b + 1, hs].contiguous(), do[b:b + 1, hs], causal, slide_size, softmax_scale)
+        lse[b:b + 1, hs], do[b:b + 1, hs], causal, window, scale)
     dq_parts = [torch.empty_like(dq_loc) for _ in range(world)]
     dist.all_gather(dq_parts, dq_loc.contiguous(), group=group)
     dq = torch.empty_like(q)
     for r in range(world):
         rb, _, rh0, rnh = head_split_assignment(B, Hq, Hkv, world, r)
         dq[rb:rb + 1, rh0:rh0 + rnh] = dq_parts[r]
-    dkv = torch.zeros((2, B, Hkv, N, D), dtype=torch.float32, device=q.device)
-    dkv[0, b, kv] = dk_loc[0, 0].float()
-    dkv[1, b, kv] = dv_loc[0, 0].float()
-    dist.all_reduce(dkv, group=group)
-    return dq, dkv[0].to(k.dtype), dkv[1].to(v.dtype)
+    dkv = torch.stack((dk_p[0, 0], dv_p[0, 0]))  # (2, N, D) fp32 partial of this rank's heads
+    if s > 1:
+        dist.all_reduce(dkv, group=_unit_subgroup(group, units, s, rank // s))
+    mine = dkv.to(k.dtype)
+    gathered = torch.empty((world,) + tuple(mine.shape), dtype=k.dtype, device=q.device)
+    dist.all_gather_into_tensor(gathered, mine, group=group)
+    dk, dv = torch.empty_like(k), torch.empty_like(v)
+    for u in range(units):
+        ub, ukv = divmod(u, Hkv)
+        dk[ub, ukv] = gathered[u * s, 0]
+        dv[ub, ukv] = gathered[u * s, 1]
+    return dq, dk, dv

@@ -143,6 +143,20 @@ GQAFA_API int gqafa_bwd_ws(const void* q, const long long* q_strides, const void
                            const long long* dv_strides, float* delta, int batch, int heads_q, int heads_kv,
                            int seqlen, int head_dim, float softmax_scale, int causal, int window, int dtype,
                            void* stream, void* workspace, long long workspace_bytes);
+/* gqafa_bwd_ws (workspace non-NULL) or gqafa_bwd (workspace NULL) with dk and
+ * dv written as fp32 (float, element strides as for the 16-bit tensors; dq
+ * stays in the input dtype). No counterpart in the reference: for callers
+ * that split the query heads of one KV group over several devices and add the
+ * partial dK / dV up (the multi-GPU head split), so that the partials are not
+ * rounded to 16 bits before the sum. */
+GQAFA_API int gqafa_bwd_partial(const void* q, const long long* q_strides, const void* k,
+                                const long long* k_strides, const void* v, const long long* v_strides,
+                                const void* o, const long long* o_strides, const void* dout,
+                                const long long* dout_strides, const float* lse, void* dq,
+                                const long long* dq_strides, void* dk, const long long* dk_strides, void* dv,
+                                const long long* dv_strides, float* delta, int batch, int heads_q, int heads_kv,
+                                int seqlen, int head_dim, float softmax_scale, int causal, int window, int dtype,
+                                void* stream, void* workspace, long long workspace_bytes);
 /* One kernel of gqafa_bwd_ws: stage 0 = dQ + delta + P/dS, 1 = dK + dV
  * (needs stage 0's workspace contents). For per-kernel timing. */
 GQAFA_API int gqafa_bwd_ws_stage(int stage, const void* q, const long long* q_strides, const void* k,

@@ -182,3 +182,42 @@ def test_noalloc_backward_matches_fp32():
     mag = torch_ref(q, k, v, do, True, 0, scale, magnitudes=True)
     for i, name, x in ((2, "dQ", dq), (3, "dK", dk), (4, "dV", dv)):
         assert_close(f"no-alloc {name}", x, ref[i], emulated=emu[i], magnitude=mag[i])
+
+
+@pytest.mark.parametrize("D,window", [(512, 0), (256, 300), (128, 0)])
+def test_partial_backward_writes_fp32_dk_dv(D, window):
+    """gqafa_bwd_partial: dK, dV in fp32 (for sums over split query heads),
+    which round to exactly the 16-bit outputs of the ordinary backward, with and
+    without a workspace."""
+    from gemma_triton_flash_attn.attention import _bwd_args
+
+    B, Hq, Hkv, N = 1, 8, 2, 700
+    q, k, v, do = make_inputs(B, Hq, Hkv, N, D, torch.bfloat16, 0.5, seed=41, device=DEV)
+    scale = 1 / math.sqrt(D)
+    o, lse = _fwd(q, k, v, True, window, scale, True)
+    size = bwd_workspace_size(B, Hq, Hkv, N, D, True, window)
+    ref = torch_ref(q, k, v, do, True, window, scale)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    for with_ws in ((True, False) if size > 0 else (False,)):
+        ws = torch.empty(size, dtype=torch.uint8, device=DEV) if with_ws else None
+        dq = torch.empty_like(q)
+        dk = torch.empty(k.shape, dtype=torch.float32, device=DEV)
+        dv = torch.empty(v.shape, dtype=torch.float32, device=DEV)
+        delta = torch.empty(B, Hq, N, device=DEV)
+        tail = (ws.data_ptr(), size) if with_ws else (None, 0)
+        _lib.check(lib.gqafa_bwd_partial(*_bwd_args(q, k, v, o, do, lse, dq, dk, dv, delta, True, window, scale,
+                                                     stream), *tail))
+        bufs = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty(B, Hq, N, device=DEV))
+        if with_ws:
+            want = _bwd(q, k, v, o, lse, do, True, window, scale, workspace=torch.empty_like(ws))
+        else:
+            for st_ in range(3):
+                _bwd(q, k, v, o, lse, do, True, window, scale, stage=st_, out=bufs)
+            want = bufs[:3]
+        torch.cuda.synchronize()
+        assert torch.equal(dq, want[0])
+        assert torch.equal(dk.to(k.dtype), want[1]) and torch.equal(dv.to(v.dtype), want[2])
+        for name, x, r in (("dK", dk, ref[3]), ("dV", dv, ref[4])):
+            err = (x - r).abs().max().item()
+            assert err <= 2e-2, f"fp32 {name} ws={with_ws}: max-abs {err:.3e}"

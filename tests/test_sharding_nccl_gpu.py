@@ -85,9 +85,9 @@ def test_sharded_equals_single_gpu(tmp_path, split, monkeypatch):
         got = torch.load(os.path.join(tmp_path, f"r{r}.pt"))
         for n, t in ref.items():
             if split == "heads" and n in ("dk", "dv"):
-                # The sum of per-rank partials, each rounded to bf16 once before the
-                # fp32 all-reduce, is held to the suite's criterion against fp32
-                # (its rounding-bound form covers the partials' extra rounding).
+                # The sum of the ranks' fp32 partials (another summation order than
+                # one GPU's, rounded once) is held to the suite's criterion
+                # against fp32.
                 assert_close(f"rank {r} {n}", got[n], ref32[n], magnitude=mag32[n])
             else:
                 d = (got[n].float() - t.float().cpu()).abs().max().item()
