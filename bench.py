@@ -75,7 +75,7 @@ def parse_args():
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="N > 1: strong = one config-4 problem over the GPUs with all-gathers (default); "
                          "weak = config 2 per GPU, no collective")
-    ap.add_argument("--gather", choices=["nccl", "ce"], default="nccl",
+    ap.add_argument("--gather", choices=["nccl", "ce"], default="ce",
                     help="N > 1 strong scaling: all-gathers by NCCL, or copy-engine pushes into symmetric memory")
     ap.add_argument("--seqlen", type=int, default=None, help="override N (not the headline)")
     ap.add_argument("--no-e2e", action="store_true")
