@@ -202,8 +202,8 @@ __device__ __forceinline__ float row_dot(const uint16_t* a, const uint16_t* b, i
   if constexpr (D >= 256) {
 #pragma unroll
     for (int it = 0; it < D / 256; ++it) {
-      const uint4 x = *reinterpret_cast<const uint4*>(a + it * 256 + lane * 8);
-      const uint4 y = *reinterpret_cast<const uint4*>(b + it * 256 + lane * 8);
+      const uint4 x = __ldg(reinterpret_cast<const uint4*>(a + it * 256 + lane * 8));
+      const uint4 y = __ldg(reinterpret_cast<const uint4*>(b + it * 256 + lane * 8));
       const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, yw[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -212,8 +212,8 @@ __device__ __forceinline__ float row_dot(const uint16_t* a, const uint16_t* b, i
       }
     }
   } else if constexpr (D == 128) {
-    const uint2 x = *reinterpret_cast<const uint2*>(a + lane * 4);
-    const uint2 y = *reinterpret_cast<const uint2*>(b + lane * 4);
+    const uint2 x = __ldg(reinterpret_cast<const uint2*>(a + lane * 4));
+    const uint2 y = __ldg(reinterpret_cast<const uint2*>(b + lane * 4));
     const uint32_t xw[2] = {x.x, x.y}, yw[2] = {y.x, y.y};
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -222,12 +222,42 @@ __device__ __forceinline__ float row_dot(const uint16_t* a, const uint16_t* b, i
     }
   } else {
     static_assert(D == 64, "head_dim");
-    const uint32_t xw = *reinterpret_cast<const uint32_t*>(a + lane * 2);
-    const uint32_t yw = *reinterpret_cast<const uint32_t*>(b + lane * 2);
+    const uint32_t xw = __ldg(reinterpret_cast<const unsigned int*>(a + lane * 2));
+    const uint32_t yw = __ldg(reinterpret_cast<const unsigned int*>(b + lane * 2));
     acc += unpack_lo<BF16>(xw) * unpack_lo<BF16>(yw);
     acc += unpack_hi<BF16>(xw) * unpack_hi<BF16>(yw);
   }
   return acc;
+}
+
+// delta = rowsum(dO o O) for rows r_first, r_first + r_step, ... < M of the
+// tile starting at query row r0 (reference: the STORE_DELTA prologue,
+// flash_attn/attention.py:733-742), one warp per row. The loads of RB rows
+// are issued before any of their reductions, so their memory latencies
+// overlap instead of adding up. Writes sRow[r] and delta[r0 + r] (rows < N).
+template <int D, bool BF16, int M>
+__device__ __forceinline__ void tile_delta(const uint16_t* Og, long long o_sn, const uint16_t* dOg, long long do_sn,
+                                           int r0, int N, int r_first, int r_step, int lane, float* sRow,
+                                           float* delta) {
+  constexpr int RB = (D >= 512) ? 2 : 4;
+  for (int r = r_first; r < M; r += RB * r_step) {
+    float acc[RB];
+#pragma unroll
+    for (int u = 0; u < RB; ++u) {
+      const int rr = r + u * r_step, q = r0 + rr;
+      acc[u] = (rr < M && q < N) ? row_dot<D, BF16>(Og + q * o_sn, dOg + q * do_sn, lane) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < RB; ++u) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
+      const int rr = r + u * r_step, q = r0 + rr;
+      if (lane == 0 && rr < M) {
+        sRow[rr] = acc[u];
+        if (q < N) delta[q] = acc[u];
+      }
+    }
+  }
 }
 
 template <bool BF16>
@@ -479,17 +509,7 @@ __global__ void __launch_bounds__(256, 1)
       // delta = rowsum(dO o O), one warp per row, coalesced 16-byte loads.
       const uint16_t* Og = reinterpret_cast<const uint16_t*>(p.o) + b * p.o_sb + h * p.o_sh;
       const uint16_t* dOg = reinterpret_cast<const uint16_t*>(p.dout) + b * p.do_sb + h * p.do_sh;
-      for (int r = q4; r < M; r += 4) {
-        const int q = r0 + r;
-        float acc = 0.f;
-        if (q < N) acc = row_dot<C::D, C::BF16>(Og + q * p.o_sn, dOg + q * p.do_sn, lane);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) {
-          sRow[r] = acc;
-          if (q < N) p.delta[rowbase_q + q] = acc;
-        }
-      }
+      tile_delta<C::D, C::BF16, M>(Og, p.o_sn, dOg, p.do_sn, r0, N, q4, 4, lane, sRow, p.delta + rowbase_q);
       asm volatile("bar.sync 1, 128;" ::: "memory");
       row_delta = sRow[srow];
       row_lse2 = (r0 + srow < N) ? p.lse[rowbase_q + r0 + srow] * LOG2E : 0.f;

@@ -428,17 +428,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(C::THREADS, 1)
     if constexpr (C::ROLE == ROLE_DQ) {
       const uint16_t* Og = reinterpret_cast<const uint16_t*>(p.o) + b * p.o_sb + h * p.o_sh;
       const uint16_t* dOg = reinterpret_cast<const uint16_t*>(p.dout) + b * p.do_sb + h * p.do_sh;
-      for (int r = rwi; r < M; r += 4 * RW) {
-        const int q = r0 + r;
-        float acc = 0.f;
-        if (q < N) acc = row_dot<C::D, C::BF16>(Og + q * p.o_sn, dOg + q * p.do_sn, lane);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) {
-          sRow[r] = acc;
-          if (q < N) p.delta[rowbase_q + q] = acc;
-        }
-      }
+      tile_delta<C::D, C::BF16, M>(Og, p.o_sn, dOg, p.do_sn, r0, N, rwi, 4 * RW, lane, sRow, p.delta + rowbase_q);
       asm volatile("bar.sync 1, %0;" ::"n"(128 * C::RW) : "memory");
       row_delta = sRow[row];
       row_lse2 = (r0 + row < N) ? p.lse[rowbase_q + r0 + row] * LOG2E : 0.f;
