@@ -82,8 +82,9 @@ struct PairCfg {
   static constexpr int KCH = SBUF_COLS / 32;  // 32-column chunks of an item per TMEM lane
   static constexpr int KCHW = KCH / RW;       // ... per row warp
 
-  static_assert(RW == 1 || RW == 2, "row warpgroups");
-  static_assert(KCH % RW == 0 && (ACC_COLS / 32) % (2 * RW) == 0 && (NACC * 4) % RW == 0, "column split");
+  static_assert(RW == 1 || RW == 2 || RW == 4, "row warpgroups");
+  static_assert(KCH % RW == 0 && (NACC * 4) % RW == 0, "column split");
+  static_assert(ROLE != ROLE_FWD || ((ACC_COLS / 32) % (2 * RW) == 0 && KCHW % 2 == 0), "forward column split");
 
   static_assert(D % 256 == 0, "D");
   static_assert(BN == 128 || BN == 256, "BN");

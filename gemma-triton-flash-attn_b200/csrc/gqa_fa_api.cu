@@ -211,7 +211,7 @@ template <bool BF16> using Dv512 = PairCfg<ROLE_DV, 512, 256, 2, 3, BF16>;
 // pair configuration with 256-key items (the recomputing path keeps the
 // 1-CTA Dq256).
 template <bool BF16> using Dkv512 = DkvCfg<512, 7, BF16>;
-template <bool BF16> using DqWs256 = PairCfg<ROLE_DQ, 256, 256, 1, 4, BF16, 2>;
+template <bool BF16> using DqWs256 = PairCfg<ROLE_DQ, 256, 256, 1, 4, BF16, 4>;
 template <bool BF16> using Dkv256 = DkvCfg<256, 7, BF16>;
 
 struct Problem {
