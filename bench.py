@@ -749,6 +749,14 @@ def run_strong(args, wl, world, rank, local):
                    pipeline="each rank copies only its own units in and out on copy streams (step s+1 upload "
                             "overlaps step s); all-gathers inside the step")
 
+    gather_kind, n_runs = att.gather, len(att.runs)
+    del att, q, k, v, do
+    torch.cuda.empty_cache()
+    try:
+        cfg2 = cfg2_over_gpus(args, world, device, stream)
+    except Exception as e:  # a secondary key must not take the headline down
+        cfg2 = dict(error=f"{type(e).__name__}: {e}"[:300])
+
     peaks = measured_peaks()
     per_rank = total / world
     if rank == 0:
@@ -760,12 +768,12 @@ def run_strong(args, wl, world, rank, local):
             config=dict(workload=wl["name"], global_batch=B, H_Q=Hq, H_KV=Hkv, N=N, D=D, causal=causal,
                         seq_len=N, units=B * Hkv, units_per_gpu=B * Hkv // world,
                         parallelism=f"{B * Hkv} (b,kv-group) units in equal blocks over {world} GPUs; "
-                                    f"O/LSE/dQ/dK/dV all-gathered ({att.gather}) inside the step",
+                                    f"O/LSE/dQ/dK/dV all-gathered ({gather_kind}) inside the step",
                         l2="inputs larger than L2 (Q, dO 1 GiB each); no flush"),
             collective=dict(ms_compute_only=round(ms_c, 3), exposed_ms=round(ms_max - ms_c, 3),
                             exposed_share=round(max(0.0, ms_max - ms_c) / ms_max, 4),
                             bytes_gathered_per_rank=round(gathered * (world - 1) / world),
-                            op=("all_gather_into_tensor x5 (NCCL, in place)" if att.gather == "nccl" else
+                            op=("all_gather_into_tensor x5 (NCCL, in place)" if gather_kind == "nccl" else
                                 "copy-engine pushes of each rank's slice into every peer's symmetric buffer x5, "
                                 "one-element NCCL all-reduce to close the step")
                             + ", overlapped with the next kernels"),
@@ -773,7 +781,7 @@ def run_strong(args, wl, world, rank, local):
                           peak=peaks["tflops_burst"], unit="TFLOP/s",
                           frac=round(per_rank / ms_max / 1e9 / peaks["tflops_burst"], 4), traffic=None),
             e2e=e2e, clocks=clocks.summary(), kernel_status=status,
-            gpu_launches=3 * len(att.runs) * args.steps,
+            gpu_launches=3 * n_runs * args.steps, cfg2_over_gpus=cfg2,
             gpu_launches_note="per rank and step: per run of units 1 forward, 1 dQ+P/dS, 1 dK+dV kernel "
                               "(plus 5 NCCL all-gathers, not counted)",
         )
@@ -805,6 +813,44 @@ def run_decoder_once(device, stream, steps=2, warmup=1):
     torch.cuda.empty_cache()
     return dict(value=round(N / (ms * 1e-3), 1), unit="tokens/s", ms_per_step=round(ms, 3),
                 workload=WORKLOADS["cfg5"]["name"])
+
+
+def cfg2_over_gpus(args, world, device, stream, steps=5, warmup=2):
+    """Config 2 (B=1, 4 (batch, KV-head) units) as one problem over the ranks:
+    unit blocks with all-gathers when the ranks divide the 4 units, else the
+    head split (the query heads of each unit over world/4 ranks, fp32 dK/dV
+    partials summed within the unit's ranks). A secondary key of the
+    multi-GPU line."""
+    from gemma_triton_flash_attn.flops import attn_flops
+    from gemma_triton_flash_attn.sharding import UnitShardedAttention, head_split_backward, head_split_forward
+
+    wl = WORKLOADS["cfg2"]
+    B, Hq, Hkv, N, D = wl["B"], wl["Hq"], wl["Hkv"], wl["N"], wl["D"]
+    units = B * Hkv
+    if units % world != 0 and (world % units != 0 or (Hq // Hkv) % (world // units) != 0):
+        return None
+    q, k, v, do = make_inputs(wl, 1234, device)
+    if units % world == 0:
+        att = UnitShardedAttention(B, Hq, Hkv, N, D, wl["dtype"], device, causal=True, gather=args.gather)
+        step = lambda: att.step(q, k, v, do)  # noqa: E731
+        how = f"(b, kv-group) units, {units // world} per GPU, all-gathers ({args.gather})"
+    else:
+        def step():
+            o, lse = head_split_forward(q, k, v, True, 0)
+            head_split_backward(q, k, v, o, lse, do, True, 0)
+        how = f"head split: {Hq // Hkv // (world // units)} query heads per GPU, fp32 dK/dV partials all-reduced " \
+              "within each unit's GPUs, outputs all-gathered (NCCL)"
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(time_loop(step, steps, stream), world, device)
+    total = attn_flops(B, Hq, N, D, True, 0, bwd=True)
+    res = dict(value=round(total / (ms * 1e-3) / 1e12, 2), unit="TFLOPS/s", ms_per_step=round(ms, 3),
+               workload=wl["name"], parallelism=how)
+    del q, k, v, do, step
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_decoder(args, wl, world, rank, local):
