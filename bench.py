@@ -822,7 +822,7 @@ def cfg2_over_gpus(args, world, device, stream, steps=5, warmup=2):
     partials summed within the unit's ranks). A secondary key of the
     multi-GPU line."""
     from gemma_triton_flash_attn.flops import attn_flops
-    from gemma_triton_flash_attn.sharding import UnitShardedAttention, head_split_backward, head_split_forward
+    from gemma_triton_flash_attn.sharding import UnitShardedAttention
 
     wl = WORKLOADS["cfg2"]
     B, Hq, Hkv, N, D = wl["B"], wl["Hq"], wl["Hkv"], wl["N"], wl["D"]
@@ -830,16 +830,13 @@ def cfg2_over_gpus(args, world, device, stream, steps=5, warmup=2):
     if units % world != 0 and (world % units != 0 or (Hq // Hkv) % (world // units) != 0):
         return None
     q, k, v, do = make_inputs(wl, 1234, device)
-    if units % world == 0:
-        att = UnitShardedAttention(B, Hq, Hkv, N, D, wl["dtype"], device, causal=True, gather=args.gather)
-        step = lambda: att.step(q, k, v, do)  # noqa: E731
+    att = UnitShardedAttention(B, Hq, Hkv, N, D, wl["dtype"], device, causal=True, gather=args.gather)
+    step = lambda: att.step(q, k, v, do)  # noqa: E731
+    if att.split == 1:
         how = f"(b, kv-group) units, {units // world} per GPU, all-gathers ({args.gather})"
     else:
-        def step():
-            o, lse = head_split_forward(q, k, v, True, 0)
-            head_split_backward(q, k, v, o, lse, do, True, 0)
-        how = f"head split: {Hq // Hkv // (world // units)} query heads per GPU, fp32 dK/dV partials all-reduced " \
-              "within each unit's GPUs, outputs all-gathered (NCCL)"
+        how = (f"head split: {Hq // Hkv // att.split} query heads per GPU, fp32 dK/dV partials all-reduced within "
+               f"each unit's {att.split} GPUs; O/LSE/dQ all-gathers ({args.gather})")
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
@@ -848,7 +845,7 @@ def cfg2_over_gpus(args, world, device, stream, steps=5, warmup=2):
     total = attn_flops(B, Hq, N, D, True, 0, bwd=True)
     res = dict(value=round(total / (ms * 1e-3) / 1e12, 2), unit="TFLOPS/s", ms_per_step=round(ms, 3),
                workload=wl["name"], parallelism=how)
-    del q, k, v, do, step
+    del q, k, v, do, step, att
     torch.cuda.empty_cache()
     return res
 

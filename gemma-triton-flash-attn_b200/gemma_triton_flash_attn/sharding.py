@@ -179,9 +179,15 @@ class UnitShardedAttention:
         dK/dV kernels -> all-gather dK, dV
         ``wait()``: the calling stream waits for the four collectives
 
-    Requires B * H_KV to be a multiple of the world size (equal blocks, which
-    the in-place all-gather needs); ``sharded_forward`` / ``sharded_backward``
-    handle the uneven case. The per-unit kernels are the materialised backward
+    Needs B * H_KV to be a multiple of the world size (equal blocks, which the
+    in-place all-gather needs), or the world size a multiple of B * H_KV with
+    the G query heads of a unit divisible by s = world / (B * H_KV): then
+    ("head split") the s ranks of a unit each take G/s of its query heads
+    (their heads are still one rank-ordered slice of the flattened storage,
+    so O, LSE and dQ are gathered the same way), each writes its dK/dV share
+    as an fp32 partial (``gqafa_bwd_partial``), the s partials are summed by
+    an all-reduce within the unit's ranks, rounded once and all-gathered.
+    ``sharded_forward`` / ``sharded_backward`` handle uneven splits. The per-unit kernels are the materialised backward
     (``gqafa_bwd_ws``) with one workspace per contiguous run of units, so the
     dQ stage of every run can precede all dK/dV stages.
 
@@ -201,15 +207,22 @@ class UnitShardedAttention:
     """
 
     def __init__(self, batch, heads_q, heads_kv, seqlen, head_dim, dtype, device, causal=True, slide_size=0,
-                 softmax_scale=None, group=None, fwd_fn=None, bwd_fn=None, gather="nccl", copy_streams=4):
+                 softmax_scale=None, group=None, fwd_fn=None, bwd_fn=None, gather="nccl", copy_streams=4,
+                 partial_fn=None):
         from .attention import _normalize_window
 
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.plan = ShardPlan(batch, heads_q, heads_kv, self.world, self.rank)
-        if self.plan.num_units % self.world != 0:
-            raise ValueError(f"{self.plan.num_units} (batch, KV-head) units do not divide over {self.world} ranks")
+        units, G = self.plan.num_units, heads_q // heads_kv
+        self.split = 1  # ranks per unit (head split when > 1)
+        if units % self.world != 0:
+            s = self.world // units
+            if self.world % units != 0 or G % s != 0:
+                raise ValueError(f"{units} (batch, KV-head) units with {G} query heads each do not divide over "
+                                 f"{self.world} ranks")
+            self.split = s
         self.shape = (batch, heads_q, heads_kv, seqlen, head_dim)
         self.causal = bool(causal)
         self.window = _normalize_window(causal, slide_size, seqlen)
@@ -238,11 +251,27 @@ class UnitShardedAttention:
                 self._peers[name] = [hdl.get_buffer(p, tuple(t.shape), t.dtype) for p in range(self.world)]
             self._copy_streams = [torch.cuda.Stream(device) for _ in range(copy_streams)]
             self._flag = torch.zeros(1, dtype=torch.int32, device=device)
-        self.runs = list(self.plan.runs())
+        if self.split == 1:
+            self.runs = list(self.plan.runs())
+        else:
+            unit, part = divmod(self.rank, self.split)
+            b, kv = divmod(unit, Hkv)
+            self.runs = [(b, kv, kv + 1)]
+            self._heads = (kv * G + part * (G // self.split), G // self.split)
+            self._unit = unit
+            self._dkv32 = torch.empty((2, 1, 1, N, D), dtype=torch.float32, device=device)
+            self._dkv_all = torch.empty((self.world, 2, N, D), dtype=dtype, device=device)
+            self._subgroup = _unit_subgroup(group, units, self.split, unit) if self.world > 1 else None
         self._fwd_fn = fwd_fn or self._kernel_fwd
         self._bwd_fn = bwd_fn or self._kernel_bwd
+        self._partial_fn = partial_fn or self._kernel_partial
         self.workspaces = None
-        if bwd_fn is None:
+        if self.split > 1 and partial_fn is None:
+            from .attention import _alloc_workspace, bwd_workspace_size
+
+            nh = self._heads[1]
+            self.workspaces = [_alloc_workspace(bwd_workspace_size(1, nh, 1, N, D, self.causal, self.window), device)]
+        elif self.split == 1 and bwd_fn is None:
             from .attention import _alloc_workspace, bwd_workspace_size
 
             G = Hq // Hkv
@@ -267,10 +296,23 @@ class UnitShardedAttention:
         _bwd(q, k, v, o, lse, do, self.causal, self.window, self.scale, stage=stage, out=(dq, dk, dv, delta),
              workspace=workspace)
 
+    def _kernel_partial(self, q, k, v, o, lse, do, dq, dk32, dv32, delta, workspace):
+        from . import _lib
+        from .attention import _bwd_args
+
+        tail = (workspace.data_ptr(), workspace.numel()) if workspace is not None else (None, 0)
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        _lib.check(_lib.load().gqafa_bwd_partial(
+            *_bwd_args(q, k, v, o, do, lse, dq, dk32, dv32, delta, self.causal, self.window, self.scale, stream),
+            *tail))
+
     # ---- slices --------------------------------------------------------------
     def _qv(self, i, t):
         """Run i's query heads of a [B, H_Q, ...] tensor (a view)."""
         b, kv0, kv1 = self.runs[i]
+        if self.split > 1:
+            h0, nh = self._heads
+            return t[b:b + 1, h0:h0 + nh]
         G = self.plan.group
         return t[b:b + 1, kv0 * G:kv1 * G]
 
@@ -313,6 +355,8 @@ class UnitShardedAttention:
     def backward(self, q, k, v, do):
         """dQ, dK, dV of this rank's units (from this rank's own O / LSE rows,
         which the all-gather does not touch), each followed by its all-gather."""
+        if self.split > 1:
+            return self._backward_head_split(q, k, v, do)
         n = len(self.runs)
         for stage in (0, 1):
             for i in range(n):
@@ -324,6 +368,21 @@ class UnitShardedAttention:
                 self._gather(self.dq, "dq")
         self._gather(self.dk, "dk")
         self._gather(self.dv, "dv")
+        return self.dq, self.dk, self.dv
+
+    def _backward_head_split(self, q, k, v, do):
+        qv, kvv = (lambda t: self._qv(0, t)), (lambda t: self._kvv(0, t))
+        ws = self.workspaces[0] if self.workspaces is not None else None
+        self._partial_fn(qv(q), kvv(k), kvv(v), qv(self.o), qv(self.lse), qv(do), qv(self.dq), self._dkv32[0],
+                         self._dkv32[1], qv(self.delta), ws)
+        self._gather(self.dq, "dq")
+        if self.world > 1:
+            dist.all_reduce(self._dkv32, group=self._subgroup)  # the unit's s partials
+            mine = self._dkv32.view(2, *self._dkv32.shape[-2:]).to(self._dkv_all.dtype)
+            out = self._dkv_all.view(-1, *self._dkv_all.shape[-2:])  # (world * 2, N, D): chunks along dim 0
+            self._works.append(dist.all_gather_into_tensor(out, mine, group=self.group, async_op=True))
+        else:
+            self._dkv_all[0].copy_(self._dkv32.view(self._dkv_all.shape[1:]))
         return self.dq, self.dk, self.dv
 
     def wait(self):
@@ -338,6 +397,12 @@ class UnitShardedAttention:
         for w in self._works:
             w.wait()
         self._works = []
+        if self.split > 1:  # one copy of each unit's summed dK, dV
+            Hkv = self.shape[2]
+            for u in range(self.plan.num_units):
+                ub, ukv = divmod(u, Hkv)
+                self.dk[ub, ukv].copy_(self._dkv_all[u * self.split, 0])
+                self.dv[ub, ukv].copy_(self._dkv_all[u * self.split, 1])
 
     def step(self, q, k, v, do):
         """One full forward + backward with every output reassembled on every rank."""

@@ -213,3 +213,52 @@ def test_unit_sharded_attention_single_rank_runs():
         assert att.runs == [(0, 0, 3), (1, 0, 3)]
     finally:
         dist.destroy_process_group()
+
+
+def _head_split_worker(rank, world, port, out_dir):
+    from gemma_triton_flash_attn.sharding import UnitShardedAttention
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        g = torch.Generator().manual_seed(9)
+        q, k, v, do = (torch.randn(s, generator=g) for s in ((1, 8, 33, 16), (1, 2, 33, 16), (1, 2, 33, 16),
+                                                             (1, 8, 33, 16)))
+
+        def fwd_fn(qs, ks, vs, o, lse):
+            oo, ll = oracle_fwd(qs, ks, vs, True, 0, None)
+            o.copy_(oo)
+            lse.copy_(ll)
+
+        def partial_fn(qs, ks, vs, o, lse, dos, dq, dk32, dv32, delta, ws):
+            gq, gk, gv = oracle_bwd(qs, ks, vs, o.clone(), lse.clone(), dos, True, 0, None)
+            dq.copy_(gq)
+            dk32.copy_(gk)  # this rank's heads' share of the KV head's gradient
+            dv32.copy_(gv)
+
+        att = UnitShardedAttention(1, 8, 2, 33, 16, torch.float32, "cpu", causal=True, fwd_fn=fwd_fn,
+                                   partial_fn=partial_fn)
+        assert att.split == world // 2
+        for _ in range(2):
+            o, lse, dq, dk, dv = att.step(q, k, v, do)
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), o=o.numpy(), lse=lse.numpy(), dq=dq.numpy(),
+                 dk=dk.numpy(), dv=dv.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_unit_sharded_attention_head_split_matches_single_rank(tmp_path, world):
+    """More ranks than (batch, KV-head) units: each unit's query heads split
+    over world / units ranks, the dK/dV partials summed within the unit's ranks."""
+    port = _free_port()
+    mp.spawn(_head_split_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+    g = torch.Generator().manual_seed(9)
+    q, k, v, do = (torch.randn(s, generator=g) for s in ((1, 8, 33, 16), (1, 2, 33, 16), (1, 2, 33, 16),
+                                                         (1, 8, 33, 16)))
+    o, lse = oracle_fwd(q, k, v, True, 0, None)
+    dq, dk, dv = oracle_bwd(q, k, v, o, lse, do, True, 0, None)
+    for r in range(world):
+        z = np.load(os.path.join(tmp_path, f"r{r}.npz"))
+        for name, ref in (("o", o), ("lse", lse), ("dq", dq), ("dk", dk), ("dv", dv)):
+            np.testing.assert_allclose(z[name], ref.numpy(), rtol=1e-5, atol=1e-5, err_msg=f"rank {r} {name}")

@@ -36,8 +36,8 @@ def _worker(rank, world, port, out_dir, split=False):
     try:
         from gemma_triton_flash_attn import sharding as sh
 
-        q, k, v, do = _inputs(f"cuda:{rank}", split in ("seq", "heads"))
-        if split in ("persistent", "persistent_ce"):
+        q, k, v, do = _inputs(f"cuda:{rank}", split in ("seq", "heads", "persistent_heads"))
+        if split in ("persistent", "persistent_ce", "persistent_heads"):
             att = sh.UnitShardedAttention(q.shape[0], q.shape[1], k.shape[1], q.shape[2], q.shape[3], q.dtype,
                                           q.device, causal=True, gather="ce" if split == "persistent_ce" else "nccl")
             for _ in range(2):  # the second step reuses every buffer
@@ -56,19 +56,19 @@ def _worker(rank, world, port, out_dir, split=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("split", [False, "persistent", "persistent_ce", "seq", "heads"],
+@pytest.mark.parametrize("split", [False, "persistent", "persistent_ce", "seq", "heads", "persistent_heads"],
                          ids=["units", "unit_sharded_attention", "unit_sharded_attention_copy_engines",
-                              "sequence_split", "head_split"])
+                              "sequence_split", "head_split", "unit_sharded_attention_head_split"])
 def test_sharded_equals_single_gpu(tmp_path, split, monkeypatch):
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs at least two GPUs")
-    if split in ("seq", "heads"):
+    if split in ("seq", "heads", "persistent_heads"):
         world = 2  # one (batch, KV-group) unit split over two ranks by sequence blocks
     from gemma_triton_flash_attn.attention import flash_attn_gqa_backward, flash_attn_gqa_forward_with_lse
 
     mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), split), nprocs=world, join=True)
-    q, k, v, do = _inputs("cuda:0", split in ("seq", "heads"))
+    q, k, v, do = _inputs("cuda:0", split in ("seq", "heads", "persistent_heads"))
     o, lse = flash_attn_gqa_forward_with_lse(q, k, v, True, 0)
     if split == "seq":
         # the sequence split runs the recomputing kernels (row-range entries):
@@ -76,7 +76,7 @@ def test_sharded_equals_single_gpu(tmp_path, split, monkeypatch):
         monkeypatch.setenv("GQAFA_BWD_WORKSPACE_LIMIT", "0")
     dq, dk, dv = flash_attn_gqa_backward(q, k, v, o, lse, do, True, 0)
     ref = dict(o=o, lse=lse, dq=dq, dk=dk, dv=dv)
-    if split == "heads":
+    if split in ("heads", "persistent_heads"):
         r32 = torch_ref(q, k, v, do, True, 0)
         m32 = torch_ref(q, k, v, do, True, 0, magnitudes=True)
         ref32 = dict(zip(("o", "lse", "dq", "dk", "dv"), r32))
@@ -84,7 +84,7 @@ def test_sharded_equals_single_gpu(tmp_path, split, monkeypatch):
     for r in range(world):
         got = torch.load(os.path.join(tmp_path, f"r{r}.pt"))
         for n, t in ref.items():
-            if split == "heads" and n in ("dk", "dv"):
+            if split in ("heads", "persistent_heads") and n in ("dk", "dv"):
                 # The sum of the ranks' fp32 partials (another summation order than
                 # one GPU's, rounded once) is held to the suite's criterion
                 # against fp32.
